@@ -1,0 +1,489 @@
+"""Benchmark: batched small-matrix exponential, forward + Frechet backward, matrices/s.
+
+Headline workload: config 5 of the benchmark set -- FP32 [1,048,576, 32, 32], entries
+N(0,1)/sqrt(32) scaled by lognormal(0,1) per matrix -- with the batch split evenly over the N
+GPUs (one process per GPU, no collective in the timed region; strong scaling).  A step is one
+forward ``fh.matrix_exp(x)`` plus one ``torch.autograd.grad(y, x, g)`` through the public API
+on the rank's shard, inputs resident in HBM (4.3 GB per tensor, larger than L2).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference package's CPU path (native torch.linalg.matrix_exp +
+autograd, flash_hypercons/ops/matrix_exp/__init__.py:26-29,95-96) on the host cores, rank 0
+only, on bounded samples of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HEADLINE = 5
+METRIC = "fwd+bwd matrices/s"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, default=HEADLINE, choices=[1, 2, 3, 4, 5])
+    p.add_argument("--no-extras", action="store_true", help="skip the secondary configs, e2e and CPU baseline")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the CPU baseline sample")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend: str):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=300))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            if torch.cuda.is_available():
+                self.pg.barrier(device_ids=[self.local_rank])
+            else:
+                self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            pass
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            if self.uuid and not parts[0].endswith(self.uuid.replace("GPU-", "")):
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ----------------------------------------------------------------------------------------
+# the step
+# ----------------------------------------------------------------------------------------
+def fwd_bwd(fh, a, g):
+    x = a.detach().requires_grad_()
+    y = fh.matrix_exp(x)
+    (grad,) = torch.autograd.grad(y, x, g)
+    return y, grad
+
+
+def count_our_launches(fh, a, g) -> int:
+    """Kernels of libfhx launched by one step, counted by the CUDA profiler."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fwd_bwd(fh, a, g)
+        torch.cuda.synchronize()
+    return sum(int(ev.count) for ev in prof.key_averages() if "fhx" in ev.key)
+
+
+def time_steps(fh, a, g, steps: int, warmup: int, dist: Dist, flush: torch.Tensor | None = None):
+    """Device time of `steps` fwd+bwd steps: total ms, and per-phase kernel ms (fwd, bwd)."""
+    for _ in range(warmup):
+        fwd_bwd(fh, a, g)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if flush is None:
+        start.record()
+        for e0, e1, e2 in ev:
+            e0.record()
+            x = a.detach().requires_grad_()
+            y = fh.matrix_exp(x)
+            e1.record()
+            torch.autograd.grad(y, x, g)
+            e2.record()
+        end.record()
+        torch.cuda.synchronize()
+        total = start.elapsed_time(end)
+    else:
+        total = 0.0
+        for e0, e1, e2 in ev:
+            flush.add_(1.0)  # write more than L2 between timed iterations
+            e0.record()
+            x = a.detach().requires_grad_()
+            y = fh.matrix_exp(x)
+            e1.record()
+            torch.autograd.grad(y, x, g)
+            e2.record()
+        torch.cuda.synchronize()
+        total = sum(e0.elapsed_time(e2) for e0, _, e2 in ev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    fwd = [e0.elapsed_time(e1) for e0, e1, _ in ev]
+    bwd = [e1.elapsed_time(e2) for _, e1, e2 in ev]
+    return total, statistics.mean(fwd), statistics.mean(bwd)
+
+
+def e2e_steps(fh, cfg, a_host, g_host, steps: int, warmup: int, dist: Dist, device):
+    """Same metric through the public API from pinned host buffers: every step copies its
+    inputs host->device, runs fwd+bwd and copies Y and the gradient back, pipelined in chunks
+    over two streams.  Returns (seconds per step, h2d bytes, d2h bytes)."""
+    batch = a_host.shape[0]
+    chunk = min(batch, 32768)
+    n = cfg.n
+    streams = [torch.cuda.Stream(device=device) for _ in range(2)]
+    dev_a = [torch.empty((chunk, n, n), dtype=cfg.dtype, device=device) for _ in range(2)]
+    dev_g = [torch.empty((chunk, n, n), dtype=cfg.dtype, device=device) for _ in range(2)]
+    y_host = torch.empty_like(a_host).pin_memory()
+    grad_host = torch.empty_like(a_host).pin_memory()
+
+    def one_step():
+        for i, lo in enumerate(range(0, batch, chunk)):
+            k = i % 2
+            s = streams[k]
+            hi = min(lo + chunk, batch)
+            with torch.cuda.stream(s):
+                xa = dev_a[k][: hi - lo]
+                xg = dev_g[k][: hi - lo]
+                xa.copy_(a_host[lo:hi], non_blocking=True)
+                xg.copy_(g_host[lo:hi], non_blocking=True)
+                src = xa.mT if cfg.transposed else xa
+                y, grad = fwd_bwd(fh, src, xg)
+                y_host[lo:hi].copy_(y.detach(), non_blocking=True)
+                grad_host[lo:hi].copy_(grad, non_blocking=True)
+        for s in streams:
+            s.synchronize()
+
+    for _ in range(warmup):
+        one_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    torch.cuda.synchronize()
+    elapsed = (time.perf_counter() - t0) / steps
+    dist.barrier()
+    nbytes = a_host.numel() * a_host.element_size()
+    return elapsed, 2 * nbytes, 2 * nbytes
+
+
+# ----------------------------------------------------------------------------------------
+# roofline
+# ----------------------------------------------------------------------------------------
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+def fp32_fma_peak_tflops(sm_count: int, mhz: float) -> float:
+    # 128 FP32 lanes per SM, one FMA (2 flops) per lane per clock.
+    return sm_count * 128 * 2 * mhz * 1e6 / 1e12
+
+
+def load_traffic(config_index: int):
+    try:
+        with open(TRAFFIC_PATH) as f:
+            data = json.load(f)
+        return data.get(str(config_index))
+    except (OSError, ValueError):
+        return None
+
+
+def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e):
+    from flash_hyperconnections_b200 import roofline as R
+    from flash_hyperconnections_b200 import workloads as W
+
+    start, count = W.shard(cfg, rank, world) if world > 1 else (0, cfg.batch)
+    a, g = W.generate(cfg, start, count, device=device)
+    torch.cuda.synchronize()
+    steps_per_matrix = R.mandated_steps(a)
+    fwd_flops = 2.0 * R.kernel_size(cfg.n) ** 3 * float(steps_per_matrix.sum().item())
+    bwd_flops = 3.0 * fwd_flops
+    in_bytes = a.numel() * a.element_size()
+    flush = None
+    if 3 * in_bytes < 256 * 2**20:  # inputs fit in L2: flush it between timed iterations
+        flush = torch.empty(64 * 2**20, dtype=torch.float32, device=device)
+    launches = count_our_launches(fh, a, g)
+    total_ms, fwd_ms, bwd_ms = time_steps(fh, a, g, steps, warmup, dist, flush)
+    result = {
+        "count": count,
+        "total_ms": total_ms,
+        "fwd_ms": fwd_ms,
+        "bwd_ms": bwd_ms,
+        "fwd_flops": fwd_flops,
+        "bwd_flops": bwd_flops,
+        "launches_per_step": launches,
+        "mean_steps": float(steps_per_matrix.double().mean().item()),
+        "bytes": R.algorithmic_bytes(count, cfg.n, cfg.elem_bytes),
+        "l2": "L2 flushed (256 MB write) between timed iterations" if flush is not None
+        else f"inputs larger than L2 ({in_bytes / 1e9:.2f} GB per tensor per rank)",
+    }
+    if with_e2e:
+        e2e_count = min(count, 131072)
+        a_host = (a[:e2e_count].mT.contiguous() if cfg.transposed else a[:e2e_count]).cpu().pin_memory()
+        g_host = g[:e2e_count].cpu().pin_memory()
+        del a, g
+        torch.cuda.empty_cache()
+        sec, h2d, d2h = e2e_steps(fh, cfg, a_host, g_host, max(2, min(steps, 5)), 1, dist, device)
+        result["e2e"] = {"sec_per_step": sec, "count": e2e_count, "h2d": h2d, "d2h": d2h}
+    return result
+
+
+# ----------------------------------------------------------------------------------------
+# CPU path of the reference (native torch + autograd on the host cores)
+# ----------------------------------------------------------------------------------------
+def cpu_reference_sample(cfg, target_seconds: float):
+    from flash_hyperconnections_b200 import workloads as W
+    from oracle import cpu_path
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    probe = 256 if cfg.n >= 16 else 2048
+    a, g = W.generate(cfg, 0, min(probe, cfg.batch), device="cpu")
+    t = cpu_path.time_fwd_bwd(a, g, repeat=1)
+    rate = a.shape[0] / t
+    count = int(min(cfg.batch, max(probe, rate * target_seconds)))
+    count = max(probe, (count // probe) * probe)
+    a, g = W.generate(cfg, 0, count, device="cpu")
+    t = cpu_path.time_fwd_bwd(a, g, repeat=1)
+    return {"value": count / t, "unit": "matrices/s", "cores": threads, "kind": "reference",
+            "sample": f"first {count} matrices of {cfg.name}: native torch.linalg.matrix_exp + autograd.grad on CPU "
+                      f"(the reference package's CPU path), {threads} threads, {t:.1f} s",
+            "seconds": t}
+
+
+def run_reference(args, dist):
+    from flash_hyperconnections_b200 import workloads as W
+    from oracle import cpu_path
+
+    cfg = W.CONFIGS[args.config]
+    if dist.rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
+    probe = 256 if cfg.n >= 16 else 2048
+    a, g = W.generate(cfg, 0, min(probe, cfg.batch), device="cpu")
+    rate = a.shape[0] / cpu_path.time_fwd_bwd(a, g, repeat=1)
+    count = int(min(cfg.batch, max(probe, rate * per_step)))
+    count = max(probe, (count // probe) * probe) if count >= probe else count
+    a, g = W.generate(cfg, 0, count, device="cpu")
+    for _ in range(args.warmup):
+        cpu_path.time_fwd_bwd(a, g, repeat=1)
+    times = [cpu_path.time_fwd_bwd(a, g, repeat=1) for _ in range(args.steps)]
+    total = sum(times)
+    value = count * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "matrices/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, config generator)",
+        "config": {"workload": cfg.name, "step_sample": count, "full_batch": cfg.batch, "n": cfg.n},
+        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": threads, "kind": "reference",
+                         "sample": f"first {count} matrices of {cfg.name} per step: native torch.linalg.matrix_exp "
+                                   f"+ autograd.grad on CPU, the reference package's CPU path"},
+        "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    dist = Dist()
+    if args.impl == "reference":
+        dist.init("gloo")
+        try:
+            run_reference(args, dist)
+        finally:
+            dist.close()
+        return
+
+    import flash_hypercons as fh
+    from flash_hyperconnections_b200 import workloads as W
+
+    device = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(device)
+    dist.init("nccl")
+    cfg = W.CONFIGS[args.config]
+    sampler = ClockSampler(dist.local_rank) if dist.rank == 0 else None
+
+    if sampler:
+        sampler.start()
+    main_res = measure_config(fh, cfg, dist.rank, dist.world, dist, args.steps, args.warmup, device,
+                              with_e2e=not args.no_extras)
+    clocks = sampler.stop() if sampler else None
+
+    total_ms = dist.max(main_res["total_ms"])
+    fwd_ms = dist.max(main_res["fwd_ms"])
+    bwd_ms = dist.max(main_res["bwd_ms"])
+    ms_per_step = total_ms / args.steps
+    value = cfg.batch / (ms_per_step / 1e3)
+    e2e = None
+    if "e2e" in main_res:
+        sec = dist.max(main_res["e2e"]["sec_per_step"])
+        e2e_total = main_res["e2e"]["count"] * dist.world
+        e2e = {"value": e2e_total / sec, "unit": "matrices/s",
+               "h2d_bytes_per_step": main_res["e2e"]["h2d"] * dist.world,
+               "d2h_bytes_per_step": main_res["e2e"]["d2h"] * dist.world,
+               "batch": e2e_total, "path": "pinned host -> fh.matrix_exp + autograd.grad -> pinned host, "
+                                           "2 streams, 32768-matrix chunks"}
+
+    extras = {}
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_extras:
+        for idx in (2, 4):
+            if idx == args.config:
+                continue
+            sub = W.CONFIGS[idx]
+            r = measure_config(fh, sub, 0, 1, dist, max(5, args.steps), args.warmup, device, with_e2e=False)
+            ms = r["total_ms"] / max(5, args.steps)
+            extras[sub.name] = {
+                "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
+                "fwd_kernel_ms": r["fwd_ms"], "bwd_kernel_ms": r["bwd_ms"],
+                "fwd_tflops": r["fwd_flops"] / (r["fwd_ms"] * 1e9), "bwd_tflops": r["bwd_flops"] / (r["bwd_ms"] * 1e9),
+                "hbm_gbs": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": r["mean_steps"], "l2": r["l2"],
+            }
+        cpu = cpu_reference_sample(cfg, args.cpu_seconds)
+
+    if dist.rank == 0:
+        peaks, peak_src = load_peaks()
+        props = torch.cuda.get_device_properties(device)
+        max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
+        fma_peak = fp32_fma_peak_tflops(props.multi_processor_count, max_mhz)
+        bwd_tflops = main_res["bwd_flops"] / (bwd_ms * 1e9)  # rank-0 shard flops over the max-rank time
+        fwd_tflops = main_res["fwd_flops"] / (fwd_ms * 1e9)
+        traffic = load_traffic(args.config)
+        roofline = {
+            "bound": "fp32_fma",
+            "kernel": "fhx::expm_team_kernel<32, Frechet> (fhx_frechet)",
+            "achieved": bwd_tflops,
+            "peak": fma_peak,
+            "unit": "TFLOP/s",
+            "frac": bwd_tflops / fma_peak,
+            "peak_source": f"nominal FP32 FMA: {props.multi_processor_count} SMs x 128 lanes x 2 flops x "
+                           f"{max_mhz:.0f} MHz (clocks.max.sm, {peak_src} MEASURED_PEAKS.json has no FP32-FMA figure)",
+            "traffic": traffic,
+            "forward": {"achieved": fwd_tflops, "frac": fwd_tflops / fma_peak},
+            "hbm": {"achieved_gbs": main_res["bytes"] / (ms_per_step * 1e6), "peak_gbs": peaks.get("hbm_gbs"),
+                    "frac": main_res["bytes"] / (ms_per_step * 1e6) / float(peaks.get("hbm_gbs", 6650.0))},
+            "flops_definition": "2 P^3 (pi(m)+s) fwd, 6 P^3 (pi(m)+s) bwd per matrix, (m, s) from the kernel's rule",
+        }
+        if clocks and clocks.get("sm_mhz"):
+            roofline["frac_at_sampled_clock"] = bwd_tflops / fp32_fma_peak_tflops(props.multi_processor_count,
+                                                                                  clocks["sm_mhz"])
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "matrices/s",
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded config generator; see flash_hyperconnections_b200/workloads.py)",
+            "config": {"workload": f"config{cfg.index}:{cfg.name} fwd+bwd", "global_batch": cfg.batch, "n": cfg.n,
+                       "io_dtype": str(cfg.dtype).replace("torch.", ""), "parallelism": f"batch shards x{dist.world}, "
+                       "no collective", "l2": main_res["l2"],
+                       "mean_products_per_matrix": main_res["mean_steps"]},
+            "gpu_launches": main_res["launches_per_step"] * args.steps,
+            "kernel_ms": {"fwd": fwd_ms / 1.0, "bwd": bwd_ms / 1.0},
+            "roofline": roofline,
+            "clocks": clocks,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = {k: v for k, v in cpu.items() if k != "seconds"}
+        if extras:
+            line["secondary_configs"] = extras
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,230 @@
+// One matrix per thread, everything in registers: the path for n <= 4.
+//
+// Each thread loads its n x n matrix (and, for the Frechet derivative, the direction E),
+// picks (m, s) from min(||A||_1, ||A||_inf), evaluates the degree-m Taylor scheme on
+// A / 2^s and squares s times.  In Frechet mode every quantity is the pair
+// (X, dX) of the block-triangular matrix [[X, dX], [0, X]], so a product costs three
+// n x n products: (X, dX)(Y, dY) = (XY, X dY + dX Y).
+//
+// Reference counterpart: the per-row warp kernel tiny::expm_kernel
+// (csrc/MatrixExpSmall.cuh:115-173), which spreads one padded 4x4/8x8 matrix over N lanes
+// and exchanges rows with one shuffle per FMA; here a thread owns a whole unpadded matrix,
+// so products need no data exchange at all.
+#pragma once
+
+#include "expm_common.cuh"
+
+namespace fhx {
+
+template <int N, bool Pair>
+struct RMat {
+  float d[N * N];
+  float u[Pair ? N * N : 1];
+};
+
+template <int N, bool Pair>
+__device__ __forceinline__ RMat<N, Pair> rmul(const RMat<N, Pair>& x, const RMat<N, Pair>& y) {
+  RMat<N, Pair> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float acc = 0.f;
+      float accu = 0.f;
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        acc = fmaf(x.d[i * N + k], y.d[k * N + j], acc);
+        if constexpr (Pair) {
+          accu = fmaf(x.d[i * N + k], y.u[k * N + j], accu);
+          accu = fmaf(x.u[i * N + k], y.d[k * N + j], accu);
+        }
+      }
+      r.d[i * N + j] = acc;
+      if constexpr (Pair) r.u[i * N + j] = accu;
+    }
+  }
+  return r;
+}
+
+// r = c0 * I
+template <int N, bool Pair>
+__device__ __forceinline__ RMat<N, Pair> rident(float c0) {
+  RMat<N, Pair> r;
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) {
+    r.d[e] = (e / N == e % N) ? c0 : 0.f;
+    if constexpr (Pair) r.u[e] = 0.f;
+  }
+  return r;
+}
+
+// r += c * x
+template <int N, bool Pair>
+__device__ __forceinline__ void raxpy(RMat<N, Pair>& r, float c, const RMat<N, Pair>& x) {
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) {
+    r.d[e] = fmaf(c, x.d[e], r.d[e]);
+    if constexpr (Pair) r.u[e] = fmaf(c, x.u[e], r.u[e]);
+  }
+}
+
+// r += x
+template <int N, bool Pair>
+__device__ __forceinline__ void radd(RMat<N, Pair>& r, const RMat<N, Pair>& x) {
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) {
+    r.d[e] += x.d[e];
+    if constexpr (Pair) r.u[e] += x.u[e];
+  }
+}
+
+// Linear combination c[0] I + c[1] b1 + c[2] b2 + ... over up to four matrices.
+template <int N, bool Pair, int K>
+__device__ __forceinline__ RMat<N, Pair> rcomb(const float (&c)[K + 1], const RMat<N, Pair>* const (&b)[K]) {
+  RMat<N, Pair> r = rident<N, Pair>(c[0]);
+#pragma unroll
+  for (int t = 0; t < K; ++t) {
+    if (c[t + 1] != 0.f) raxpy(r, c[t + 1], *b[t]);
+  }
+  return r;
+}
+
+// Degree-m Taylor scheme of Bader-Blanes-Casas (2019) on an already scaled matrix.
+template <int N, bool Pair>
+__device__ __forceinline__ RMat<N, Pair> taylor(int m, const RMat<N, Pair>& a) {
+  using M = RMat<N, Pair>;
+  if (m == 1) {
+    M r = rident<N, Pair>(1.f);
+    radd(r, a);
+    return r;
+  }
+  const M a2 = rmul(a, a);
+  if (m == 2) {
+    M r = rident<N, Pair>(1.f);
+    radd(r, a);
+    raxpy(r, 0.5f, a2);
+    return r;
+  }
+  if (m == 4) {
+    M c = rident<N, Pair>(0.5f);
+    raxpy(c, 1.f / 6.f, a);
+    raxpy(c, 1.f / 24.f, a2);
+    M r = rmul(a2, c);
+    M f = rident<N, Pair>(1.f);
+    radd(f, a);
+    radd(r, f);
+    return r;
+  }
+  if (m == 8) {
+    M c1 = rident<N, Pair>(0.f);
+    raxpy(c1, kT8X1, a);
+    raxpy(c1, kT8X2, a2);
+    const M a4 = rmul(a2, c1);
+    M left = a4;
+    raxpy(left, kT8X3, a2);
+    M right = rident<N, Pair>(kT8X4);
+    raxpy(right, kT8X5, a);
+    raxpy(right, kT8X6, a2);
+    raxpy(right, kT8X7, a4);
+    M r = rmul(left, right);
+    M f = rident<N, Pair>(1.f);
+    radd(f, a);
+    raxpy(f, kT8Y2, a2);
+    radd(r, f);
+    return r;
+  }
+  const M a3 = rmul(a2, a);
+  if (m == 12) {
+    const M* basis[3] = {&a, &a2, &a3};
+    const float c1[4] = {t12c(0, 0), t12c(0, 1), t12c(0, 2), t12c(0, 3)};
+    const float c2[4] = {t12c(1, 0), t12c(1, 1), t12c(1, 2), t12c(1, 3)};
+    const float c3[4] = {t12c(2, 0), t12c(2, 1), t12c(2, 2), t12c(2, 3)};
+    const float c4[4] = {t12c(3, 0), t12c(3, 1), t12c(3, 2), t12c(3, 3)};
+    const M b4 = rcomb<N, Pair, 3>(c4, basis);
+    M a6 = rmul(b4, b4);
+    radd(a6, rcomb<N, Pair, 3>(c3, basis));
+    M left = rcomb<N, Pair, 3>(c2, basis);
+    radd(left, a6);
+    M r = rmul(left, a6);
+    radd(r, rcomb<N, Pair, 3>(c1, basis));
+    return r;
+  }
+  const M a6 = rmul(a3, a3);
+  const M* basis[4] = {&a, &a2, &a3, &a6};
+  const float c1[5] = {t18c(0, 0), t18c(0, 1), t18c(0, 2), t18c(0, 3), t18c(0, 4)};
+  const float c2[5] = {t18c(1, 0), t18c(1, 1), t18c(1, 2), t18c(1, 3), t18c(1, 4)};
+  const float c3[5] = {t18c(2, 0), t18c(2, 1), t18c(2, 2), t18c(2, 3), t18c(2, 4)};
+  const float c4[5] = {t18c(3, 0), t18c(3, 1), t18c(3, 2), t18c(3, 3), t18c(3, 4)};
+  const float c5[5] = {t18c(4, 0), t18c(4, 1), t18c(4, 2), t18c(4, 3), t18c(4, 4)};
+  M a9 = rmul(rcomb<N, Pair, 4>(c1, basis), rcomb<N, Pair, 4>(c5, basis));
+  radd(a9, rcomb<N, Pair, 4>(c4, basis));
+  M left = rcomb<N, Pair, 4>(c3, basis);
+  radd(left, a9);
+  M r = rmul(left, a9);
+  radd(r, rcomb<N, Pair, 4>(c2, basis));
+  return r;
+}
+
+template <int N, bool Pair>
+__global__ void __launch_bounds__(128) expm_reg_kernel(View a, View e, void* __restrict__ out, int64_t batch,
+                                                       int dtype) {
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  RMat<N, Pair> x;
+  bool bad = false;
+  double col[N], row[N];
+#pragma unroll
+  for (int t = 0; t < N; ++t) col[t] = row[t] = 0.0;
+  const int64_t abase = b * a.s0;
+  const int64_t ebase = b * e.s0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = a.sign * load_elem(a.data, dtype, abase + i * a.s1 + j * a.s2);
+      x.d[i * N + j] = v;
+      bad |= !isfinite(v);
+      const double av = fabs(double(v));
+      col[j] += av;
+      row[i] += av;
+      if constexpr (Pair) {
+        const float w = e.sign * load_elem(e.data, dtype, ebase + i * e.s1 + j * e.s2);
+        x.u[i * N + j] = w;
+        bad |= !isfinite(w);
+      }
+    }
+  }
+  const int64_t obase = b * (N * N);
+  if (bad) {
+#pragma unroll
+    for (int t = 0; t < N * N; ++t) store_elem(out, dtype, obase + t, __int_as_float(0x7fc00000));
+    return;
+  }
+  double n1 = 0.0, ninf = 0.0;
+#pragma unroll
+  for (int t = 0; t < N; ++t) {
+    n1 = fmax(n1, col[t]);
+    ninf = fmax(ninf, row[t]);
+  }
+  int m, s;
+  choose_degree(fmin(n1, ninf), &m, &s);
+  if (s > 0) {
+#pragma unroll
+    for (int t = 0; t < N * N; ++t) {
+      x.d[t] = scale_pow2(x.d[t], s);
+      if constexpr (Pair) x.u[t] = scale_pow2(x.u[t], s);
+    }
+  }
+  RMat<N, Pair> r = taylor<N, Pair>(m, x);
+  for (int t = 0; t < s; ++t) r = rmul(r, r);
+#pragma unroll
+  for (int t = 0; t < N * N; ++t) {
+    if constexpr (Pair) {
+      store_elem(out, dtype, obase + t, r.u[t]);
+    } else {
+      store_elem(out, dtype, obase + t, r.d[t]);
+    }
+  }
+}
+
+}  // namespace fhx

@@ -1,0 +1,164 @@
+// C ABI of the batched small-matrix exponential: argument checks, kernel selection and
+// launch geometry.  Declarations and status codes: include/fhx.h.
+//
+// Reference counterpart: the host launcher small_matrix_exp_cuda (csrc/matrix_exp.cu:51-78)
+// with launch_small_matrix_exp (:13-33).  There, every call first materialises a
+// contiguous FP32 copy of the input (and of the direction), zero-padded to 4/8/16/32, and
+// un-pads the output with another copy; here the kernels read any strided view in the I/O
+// dtype directly and write the n x n output once.
+#include <mutex>
+
+#include "expm_common.cuh"
+#include "expm_reg.cuh"
+#include "expm_team.cuh"
+#include "fhx.h"
+
+namespace fhx {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kTeamWarps = 2;
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+};
+
+std::mutex g_mutex;
+DeviceInfo g_devices[kMaxDevices];
+
+// Per-(kernel, device) launch geometry: resident CTAs per SM at the kernel's smem size.
+struct LaunchShape {
+  bool ready[kMaxDevices] = {};
+  int blocks_per_sm[kMaxDevices] = {};
+};
+
+int device_sms(int dev) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceInfo& d = g_devices[dev];
+  if (!d.ready) {
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    d.ready = true;
+  }
+  return d.sms;
+}
+
+template <typename Kernel>
+int resident_blocks(Kernel kernel, LaunchShape& shape, int dev, int threads, size_t smem) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!shape.ready[dev]) {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+      return -1;
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem) != cudaSuccess) return -1;
+    shape.blocks_per_sm[dev] = blocks > 0 ? blocks : 1;
+    shape.ready[dev] = true;
+  }
+  return shape.blocks_per_sm[dev];
+}
+
+template <int N, bool Pair>
+int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype, cudaStream_t stream) {
+  constexpr int threads = 128;
+  const int64_t blocks = (batch + threads - 1) / threads;
+  if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
+  expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, batch, dtype);
+  return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
+}
+
+template <int P, bool Pair>
+int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
+  using C = TeamCfg<P, Pair>;
+  static LaunchShape shape;
+  constexpr int threads = kTeamWarps * 32;
+  constexpr size_t smem = size_t(kTeamWarps) * C::WARP_FLOATS * sizeof(float);
+  auto kernel = expm_team_kernel<P, Pair, kTeamWarps>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
+  const int sms = device_sms(dev);
+  const int per_sm = resident_blocks(kernel, shape, dev, threads, smem);
+  if (sms <= 0 || per_sm <= 0) return FHX_ERR_CUDA;
+  const int64_t items = (batch + C::TPW - 1) / C::TPW;
+  const int64_t needed = (items + kTeamWarps - 1) / kTeamWarps;
+  const int64_t resident = int64_t(sms) * per_sm;
+  const int blocks = int(needed < resident ? needed : resident);
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, batch, n, dtype);
+  return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
+}
+
+template <bool Pair>
+int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
+  switch (n) {
+    case 2: return launch_reg<2, Pair>(a, e, out, batch, dtype, stream);
+    case 3: return launch_reg<3, Pair>(a, e, out, batch, dtype, stream);
+    case 4: return launch_reg<4, Pair>(a, e, out, batch, dtype, stream);
+    default: break;
+  }
+  if (n <= 8) return launch_team<8, Pair>(a, e, out, batch, n, dtype, stream);
+  if (n <= 16) return launch_team<16, Pair>(a, e, out, batch, n, dtype, stream);
+  return launch_team<32, Pair>(a, e, out, batch, n, dtype, stream);
+}
+
+int check_common(int64_t batch, int32_t n, int32_t dtype, const void* out) {
+  if (n < 2 || n > FHX_MAX_N || batch < 0) return FHX_ERR_SIZE;
+  if (dtype != FHX_DTYPE_F32 && dtype != FHX_DTYPE_BF16 && dtype != FHX_DTYPE_F16) return FHX_ERR_DTYPE;
+  if (batch > 0 && out == nullptr) return FHX_ERR_POINTER;
+  return FHX_OK;
+}
+
+int check_view(const void* p, int64_t s0, int64_t s1, int64_t s2, int64_t batch) {
+  if (batch > 0 && p == nullptr) return FHX_ERR_POINTER;
+  if (s0 < 0 || s1 < 0 || s2 < 0) return FHX_ERR_STRIDE;
+  return FHX_OK;
+}
+
+}  // namespace
+}  // namespace fhx
+
+extern "C" {
+
+int32_t fhx_matrix_exp(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                       void* output, int64_t batch, int32_t n, int32_t dtype, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View none{nullptr, 0, 0, 0, 1.f};
+  return dispatch<false>(a, none, output, batch, n, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                    const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
+                    void* output, int64_t batch, int32_t n, int32_t dtype, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  st = check_view(direction, dir_s0, dir_s1, dir_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View e{direction, dir_s0, dir_s1, dir_s2, dir_negate ? -1.f : 1.f};
+  return dispatch<true>(a, e, output, batch, n, dtype, static_cast<cudaStream_t>(stream));
+}
+
+const char* fhx_status_string(int32_t status) {
+  switch (status) {
+    case FHX_OK: return "ok";
+    case FHX_ERR_SIZE: return "expected 2 <= n <= 32 and batch >= 0";
+    case FHX_ERR_DTYPE: return "dtype must be float32, bfloat16 or float16";
+    case FHX_ERR_POINTER: return "null data pointer for a non-empty batch";
+    case FHX_ERR_STRIDE: return "negative stride";
+    case FHX_ERR_CUDA: return "CUDA launch failed";
+    default: return "unknown status";
+  }
+}
+
+int32_t fhx_abi_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,151 @@
+"""Python operator layer: eligibility, native routing, autograd, fake kernels, scoped routing.
+
+Behaviour mirrors flash_hypercons/ops/matrix_exp/__init__.py of the reference package
+(file:lines cited per function) so that code written against ``flash_hypercons`` runs
+unchanged.  The operators themselves are registered in C++ (``csrc/torch_ops.cpp``) and
+launch the sm_100a kernels of ``libfhx.so``.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch.overrides import TorchFunctionMode, has_torch_function
+
+from ... import _C  # noqa: F401  (registers flash_hypercons::_matrix_exp / _frechet)
+
+_NATIVE = torch.ops.aten.linalg_matrix_exp.default
+_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+_ROUTED = (torch.linalg.matrix_exp, torch.matrix_exp, torch.Tensor.matrix_exp)
+_MAX_N = 32
+
+
+def _eligible(input: torch.Tensor) -> bool:
+    """Kernel eligibility (reference __init__.py:13-23): a strided NVIDIA CUDA [B, N, N]
+    tensor with 2 <= N <= 32 in float32 / float16 / bfloat16."""
+    if not isinstance(input, torch.Tensor):
+        return False
+    if input.device.type != "cuda" or torch.version.hip is not None:
+        return False
+    if input.layout != torch.strided or input.ndim != 3:
+        return False
+    n = input.shape[-1]
+    return input.shape[-2] == n and 1 < n <= _MAX_N and input.dtype in _DTYPES
+
+
+def _native(input: torch.Tensor, *, promote: bool = False) -> torch.Tensor:
+    """Native PyTorch exponential; CUDA half types are computed in float32 when ``promote``
+    (reference __init__.py:26-29)."""
+    if promote and input.is_cuda and input.dtype in (torch.float16, torch.bfloat16):
+        return _NATIVE(input.float()).to(input.dtype)
+    return _NATIVE(input)
+
+
+def _frechet_reference(input: torch.Tensor, direction: torch.Tensor) -> torch.Tensor:
+    """Differentiable L(input, direction) as the upper-right block of the native exponential of
+    [[A, E], [0, A]] in float32 (reference __init__.py:32-37); used when a graph of the
+    backward itself is needed."""
+    n = input.shape[-1]
+    a = input.float()
+    e = direction.float()
+    top = torch.cat((a, e), dim=-1)
+    bottom = torch.cat((torch.zeros_like(a), a), dim=-1)
+    return _NATIVE(torch.cat((top, bottom), dim=-2))[..., :n, n:].to(input.dtype)
+
+
+@torch.library.register_fake("flash_hypercons::_matrix_exp")
+def _matrix_exp_fake(input):
+    # Same metadata checks as the reference fake (__init__.py:40-49).
+    torch._check(input.device.type == "cuda")
+    torch._check(input.layout == torch.strided)
+    torch._check(input.ndim == 3)
+    torch._check(input.dtype in _DTYPES)
+    torch._check(input.shape[-1] == input.shape[-2])
+    torch._check(input.shape[-1] > 1)
+    torch._check(input.shape[-1] <= _MAX_N)
+    return input.new_empty(input.shape)
+
+
+@torch.library.register_fake("flash_hypercons::_frechet")
+def _frechet_fake(input, direction):
+    # Reference __init__.py:52-58.
+    torch._check(direction.shape == input.shape)
+    torch._check(direction.device == input.device)
+    torch._check(direction.dtype == input.dtype)
+    torch._check(direction.layout == torch.strided)
+    return _matrix_exp_fake(input)
+
+
+def _setup_context(ctx, inputs, output):
+    # Only the input is kept; the backward recomputes the powers in-kernel
+    # (reference __init__.py:61-62).
+    ctx.save_for_backward(inputs[0])
+
+
+def _needs_differentiable_backward(input, grad_output) -> bool:
+    return (
+        torch.is_grad_enabled()
+        or has_torch_function((input, grad_output))
+        or torch.autograd.forward_ad.unpack_dual(input).tangent is not None
+        or torch.autograd.forward_ad.unpack_dual(grad_output).tangent is not None
+    )
+
+
+def _backward(ctx, grad_output):
+    """dL/dA = L(A^T, dL/dY) (reference __init__.py:65-74).  ``input.mT`` is a strided view:
+    the kernel reads it through its swapped strides, no transposed copy is made."""
+    (input,) = ctx.saved_tensors
+    if _needs_differentiable_backward(input, grad_output):
+        return _frechet_reference(input.mT, grad_output)
+    return torch.ops.flash_hypercons._frechet(input.mT, grad_output)
+
+
+torch.library.register_autograd("flash_hypercons::_matrix_exp", _backward, setup_context=_setup_context)
+
+
+def matrix_exp(input: torch.Tensor) -> torch.Tensor:
+    """Compute exp(input), accelerating CUDA [B, N, N] tensors with 2 <= N <= 32.
+
+    The CUDA implementation accepts float32, float16, and bfloat16. Other
+    inputs use native PyTorch. Forward AD, function transforms, and tensor
+    subclasses also use native operations; their CUDA low-precision inputs
+    are promoted to float32 for the calculation and cast back on return.
+    """
+    # Transforms are checked before shape eligibility: vmap can hide batch dimensions
+    # (reference __init__.py:88-97).
+    if isinstance(input, torch.Tensor) and (
+        type(input) not in (torch.Tensor, torch.nn.Parameter)
+        or torch._C._are_functorch_transforms_active()
+        or torch.autograd.forward_ad.unpack_dual(input).tangent is not None
+    ):
+        return _native(input, promote=True)
+    if not _eligible(input):
+        return _native(input)
+    return torch.ops.flash_hypercons._matrix_exp(input)
+
+
+class _MatrixExpMode(TorchFunctionMode):
+    """Routes the three Python matrix-exp entry points to ``matrix_exp`` when called with a
+    single tensor (positionally or as ``input=``); everything else passes through unchanged
+    (reference __init__.py:100-108)."""
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if func in _ROUTED:
+            if len(args) == 1 and not kwargs:
+                return matrix_exp(args[0])
+            if not args and set(kwargs) == {"input"}:
+                return matrix_exp(kwargs["input"])
+        return func(*args, **kwargs)
+
+
+def use_backend() -> TorchFunctionMode:
+    """Route Python matrix-exp calls through flash-hypercons within a with block.
+
+    Scopes nest and restore normal routing on exit, including exceptional exit.
+    Enter the scope around calls to compiled functions as well as eager calls.
+    Direct ATen/C++ calls are unaffected.
+    """
+    return _MatrixExpMode()
+
+
+__all__ = ["matrix_exp", "use_backend"]

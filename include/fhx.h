@@ -1,0 +1,78 @@
+/*
+ * fhx.h -- C ABI of the B200 batched small-matrix exponential (libfhx.so).
+ *
+ * Plain pointers, element strides and sizes; no framework types.  Every entry point
+ * launches asynchronously on the given CUDA stream of the *current* device and returns a
+ * status code (FHX_OK on success).  Inputs are read-only, the output is written in full,
+ * nothing is retained between calls and no device memory is allocated.
+ *
+ * Reference interfaces these replace (nickjeliopoulos/flash-hyperconnections):
+ *   fhx_matrix_exp  <- op schema  flash_hypercons::_matrix_exp(Tensor input) -> Tensor
+ *                      (csrc/register.cpp:11, CUDA impl csrc/register.cpp:16,
+ *                       host launcher csrc/matrix_exp.cu:80-82 -> :51-78)
+ *   fhx_frechet     <- op schema  flash_hypercons::_frechet(Tensor input, Tensor direction) -> Tensor
+ *                      (csrc/register.cpp:12, CUDA impl csrc/register.cpp:17,
+ *                       host launcher csrc/matrix_exp.cu:84-86 -> :51-78)
+ * The argument checks of csrc/matrix_exp.cu:52-58 map to FHX_ERR_* codes below; the
+ * reference's pre-copies (dtype cast, contiguous, resolve_neg, zero padding,
+ * csrc/matrix_exp.cu:35-44,77) are replaced by the strides/negate arguments, which the
+ * kernels honour in their load path.
+ */
+#ifndef FHX_H_
+#define FHX_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of input, direction and output (all three share it). */
+#define FHX_DTYPE_F32 0
+#define FHX_DTYPE_BF16 1
+#define FHX_DTYPE_F16 2
+
+/* Status codes. */
+#define FHX_OK 0
+#define FHX_ERR_SIZE 1       /* n outside [2, 32] or batch < 0                          */
+#define FHX_ERR_DTYPE 2      /* dtype not one of FHX_DTYPE_*                            */
+#define FHX_ERR_POINTER 3    /* null data pointer with batch > 0                        */
+#define FHX_ERR_STRIDE 4     /* negative stride                                         */
+#define FHX_ERR_CUDA 5       /* a CUDA runtime call or the kernel launch failed         */
+
+#define FHX_MAX_N 32
+
+/*
+ * Y = exp(A) for a batch of n x n matrices, 2 <= n <= 32.
+ *   input            A, element (b, i, j) at input[b*in_s0 + i*in_s1 + j*in_s2]
+ *   in_negate        non-zero: use -A (a lazily negated view)
+ *   output           contiguous [batch, n, n], same dtype
+ *   stream           a cudaStream_t (NULL = legacy default stream)
+ * Any non-finite entry of a matrix makes that matrix's whole output NaN.
+ */
+int32_t fhx_matrix_exp(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                       void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
+
+/*
+ * Frechet derivative L(A, E) = d/dt exp(A + tE) at t = 0 (the upper-right block of
+ * exp([[A, E], [0, A]])).  The autograd backward of Y = exp(X) is
+ * fhx_frechet(X^T, dY), obtained by passing X's strides with in_s1/in_s2 swapped.
+ * The Taylor degree and the number of squarings depend on A only and are identical for A
+ * and A^T, so the backward repeats the forward's choice.
+ * Any non-finite entry of A or E makes that matrix's whole output NaN.
+ */
+int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                    const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
+                    void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
+
+/* Static description of a status code. */
+const char* fhx_status_string(int32_t status);
+
+/* ABI version of this library (major * 100 + minor). */
+int32_t fhx_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FHX_H_ */

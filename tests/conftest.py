@@ -1,0 +1,32 @@
+import os
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+HAS_GPU = torch.cuda.is_available() and torch.version.hip is None
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an NVIDIA GPU (B200, sm_100a)")
+    config.addinivalue_line("markers", "compile: exercises torch.compile")
+    config.addinivalue_line("markers", "slow: long-running")
+
+
+def pytest_collection_modifyitems(items):
+    if HAS_GPU:
+        return
+    skip = pytest.mark.skip(reason="requires an NVIDIA GPU")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def seed():
+    # Same seed as the reference test-suite (tests/conftest.py:13-15 of flash_hypercons).
+    torch.manual_seed(9041)

@@ -1,0 +1,75 @@
+"""Tolerance checks on the five benchmark configurations against the float64 oracle.
+
+Stated tolerance: relative Frobenius error of the whole checked batch <= 1e-5 for float32 and
+<= 1e-2 for bfloat16/float16, for both Y = exp(A) and the input gradient L(A^T, G).  The
+per-matrix criterion of the reference tests must hold as well.  The oracle runs on a seeded
+prefix of each config; the full-size batch is then covered by size-independent properties:
+every output finite, bit-identical to the prefix-only run on the shared prefix (batch
+invariance, so the checked prefix is exactly what the full run computed), and for the
+skew-symmetric config ||Y^T Y - I|| small over the whole batch.
+"""
+
+import pytest
+import torch
+
+import flash_hypercons as fh
+from flash_hyperconnections_b200 import workloads as W
+from oracle import expm_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+PREFIX = {1: 128, 2: 8192, 3: 8192, 4: 2048, 5: 1024}
+REL_FRO_TOL = {torch.float32: 1e-5, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+
+
+def _fwd_bwd(a, g):
+    x = a.detach().requires_grad_()
+    y = fh.matrix_exp(x)
+    (grad,) = torch.autograd.grad(y, x, g)
+    return y.detach(), grad
+
+
+@pytest.mark.parametrize("index", [1, 2, 3, 4, 5])
+def test_config_tolerance(index):
+    cfg = W.CONFIGS[index]
+    a, g = W.generate(cfg, 0, PREFIX[index], device="cuda")
+    if cfg.transposed:
+        assert not a.is_contiguous() and a.mT.is_contiguous()
+    y, grad = _fwd_bwd(a, g)
+    ref_y = O.exp_fp64(a)
+    ref_g = O.frechet_fp64(a.mT, g)
+    tol = REL_FRO_TOL[cfg.dtype]
+    fro_y, per_y = O.rel_frobenius(y, ref_y)
+    fro_g, per_g = O.rel_frobenius(grad, ref_g)
+    print(f"config {index}: rel-Frobenius Y {fro_y:.3e} (per-matrix p50 {per_y.median():.2e} max {per_y.max():.2e}); "
+          f"grad {fro_g:.3e} (p50 {per_g.median():.2e} max {per_g.max():.2e})")
+    assert fro_y <= tol, fro_y
+    assert fro_g <= tol, fro_g
+    kind = "float32" if cfg.dtype == torch.float32 else "half"
+    assert O.per_matrix_error(y, ref_y).max() <= O.tolerance(kind, False)
+    assert O.per_matrix_error(grad, ref_g).max() <= O.tolerance(kind, True)
+    if index == 4:
+        yd = y.double()
+        ortho = (yd.mT @ yd - torch.eye(cfg.n, device="cuda", dtype=torch.float64)).abs().amax()
+        assert ortho <= 2e-2, ortho
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("index", [2, 3, 4, 5])
+def test_config_full_size_properties(index):
+    cfg = W.CONFIGS[index]
+    a, g = W.generate(cfg, 0, cfg.batch, device="cuda")
+    y, grad = _fwd_bwd(a, g)
+    assert y.isfinite().all() and grad.isfinite().all()
+    k = PREFIX[index]
+    y_pre, grad_pre = _fwd_bwd(a[:k], g[:k])
+    torch.testing.assert_close(y[:k], y_pre, atol=0, rtol=0)
+    torch.testing.assert_close(grad[:k], grad_pre, atol=0, rtol=0)
+    if index == 4:
+        ortho = torch.zeros((), device="cuda", dtype=torch.float64)
+        for lo in range(0, cfg.batch, 65536):
+            yd = y[lo : lo + 65536].double()
+            ortho = torch.maximum(ortho, (yd.mT @ yd - torch.eye(cfg.n, device="cuda", dtype=torch.float64)).abs().amax())
+        assert ortho <= 2e-2, ortho
+    del y, grad, a, g
+    torch.cuda.empty_cache()
