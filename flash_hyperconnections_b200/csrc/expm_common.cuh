@@ -20,9 +20,27 @@ struct View {
   float sign;
 };
 
+// Global loads are volatile asm: the compiler may neither re-issue them at their point of
+// use nor move them, so a load issued ahead of time stays in flight (prefetch).
+__device__ __forceinline__ float ld_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned short ld_u16(const unsigned short* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_f32x4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t off) {
-  if (dtype == kF32) return __ldg(static_cast<const float*>(p) + off);
-  const unsigned short raw = __ldg(static_cast<const unsigned short*>(p) + off);
+  if (dtype == kF32) return ld_f32(static_cast<const float*>(p) + off);
+  const unsigned short raw = ld_u16(static_cast<const unsigned short*>(p) + off);
   if (dtype == kBF16) return __bfloat162float(__ushort_as_bfloat16(raw));
   return __half2float(__ushort_as_half(raw));
 }
@@ -34,6 +52,26 @@ __device__ __forceinline__ void store_elem(void* p, int dtype, int64_t off, floa
     static_cast<__nv_bfloat16*>(p)[off] = __float2bfloat16_rn(v);
   } else {
     static_cast<__half*>(p)[off] = __float2half_rn(v);
+  }
+}
+
+// Four consecutive output elements at element offset off (16-byte aligned for float32,
+// 8-byte aligned for the half types).
+__device__ __forceinline__ void store_chunk(void* p, int dtype, int64_t off, float4 v) {
+  if (dtype == kF32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + off) = v;
+  } else if (dtype == kBF16) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 w;
+    w.x = *reinterpret_cast<const unsigned*>(&lo);
+    w.y = *reinterpret_cast<const unsigned*>(&hi);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + off) = w;
+  } else {
+    const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+    uint2 w;
+    w.x = *reinterpret_cast<const unsigned*>(&lo);
+    w.y = *reinterpret_cast<const unsigned*>(&hi);
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p) + off) = w;
   }
 }
 
@@ -68,7 +106,17 @@ __host__ __device__ __forceinline__ void choose_degree(double nu, int* m, int* s
   }
 }
 
-// x * 2^-s without forming a subnormal multiplier for large s.
-__device__ __forceinline__ float scale_pow2(float x, int s) { return ldexpf(x, -s); }
+// x * 2^-s (s >= 0) by multiplications with exact, normal powers of two.
+__device__ __forceinline__ float scale_pow2(float x, int s) {
+  const int s1 = s < 126 ? s : 126;
+  float r = x * __int_as_float((127 - s1) << 23);
+  int rest = s - s1;
+  while (rest > 0) {
+    const int k = rest < 126 ? rest : 126;
+    r *= __int_as_float((127 - k) << 23);
+    rest -= k;
+  }
+  return r;
+}
 
 }  // namespace fhx

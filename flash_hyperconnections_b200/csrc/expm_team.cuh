@@ -1,375 +1,565 @@
 // Team kernel: padded sizes P = 8, 16, 32 (n = 5..32).
 //
-// A "team" of T = (P/4) * (P/8) lanes owns one matrix; lane (rb, cb) owns the 4 x 8 register
-// tile at rows 4rb.., columns 8cb...  P = 32 is one matrix per warp, P = 16 four, P = 8
-// sixteen.  Every polynomial step and every squaring is one product C = X Y (+ Z) of two
-// shared-memory planes, computed as a register-tiled outer product: per k a lane reads 4
-// values of column k of X and 8 of row k of Y (two 128-bit loads) for 32 FMAs (96 in
-// Frechet mode, where (X, dX)(Y, dY) = (XY, X dY + dX Y)).  Planes are row-major with the
-// 16-byte chunks of row i rotated by (i / 4), so the column reads of different row blocks
-// fall in different banks and the row reads stay 16-byte aligned.
+// A "team" of T = (P/4) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
+// the 4 x TN register tile at rows 4rb.., columns TN*cb...  TN = 8 or 4 per configuration,
+// so a team is 2..32 lanes of one warp or, for the 32 x 32 Frechet derivative, two warps.
+// The matrix state lives in five shared-memory plane slots per team; registers hold only
+// the accumulator tile of the product in flight.
 //
-// Degree schemes (m = 2..18) are "step programs" over four plane slots s0..s3 and one
-// register tile Z: each step is a product followed by a lane-local epilogue that forms
-// the next operands as linear combinations of the powers.  All teams of a warp execute
-// the product loop in lockstep (one __syncwarp after the product, one after the
-// epilogue); a team whose own program is shorter simply idles, so every matrix gets
-// exactly its own (m, s) and the result of a matrix never depends on its neighbours.
+// Every polynomial step and every squaring is one product R = X Y (+ Z) of slots X, Y (Z an
+// optional slot added on the way in), computed as a register-tiled outer product: per four
+// k a thread reads the 4 x 4 block of X it needs (four 128-bit loads) and per k the TN
+// values of row k of Y (TN/4 128-bit loads) for 4 TN FMAs -- three times that in Frechet
+// mode, where every matrix is the pair (M, dM) of the block-triangular [[M, dM], [0, M]] and
+// (X, dX)(Y, dY) = (XY, X dY + dX Y).  Planes are row-major with the 16-byte chunks of row i
+// rotated by i/4, so the block reads of different row blocks hit different bank groups while
+// every chunk stays 16-byte aligned.
 //
-// Work is persistent: grid = resident CTAs, warp w takes warp items w, w + W, ...
+// The degree-m schemes are table-driven "step programs" (kSteps below): after each product
+// the thread writes R into a slot and applies a short list of element-wise linear
+// combinations to its own tile (the next operands of the scheme).  Teams sharing a warp run
+// the product loop in lockstep with a barrier after the product and after the epilogue; a
+// team whose program (pi(m) + s steps) is shorter idles, so every matrix is computed with
+// exactly its own (m, s) and its result never depends on its neighbours.  The code is kept
+// compact on purpose: a fully unrolled per-degree epilogue overflows the instruction cache
+// (measured: instruction-fetch stalls dominated an earlier unrolled version).
 //
-// Reference counterpart: scalar::tiled_kernel (csrc/MatrixExpSmall.cuh:177-385), one CTA
-// per padded 16x16/32x32 matrix with 2-8 elements per thread, operands restaged through
-// shared memory with two __syncthreads per product and a fixed degree 18.
+// Loads and stores are line-per-thread: thread t of a team moves rows t, t + T, ... of the
+// matrix between global memory (any strides, three dtypes) and slot 0, accumulating the row
+// sums of |A| on the way; the column sums are read back from the slot.
+//
+// Work is persistent: grid = resident CTAs, CTA c takes CTA items c, c + gridDim.x, ...
+//
+// Reference counterpart: scalar::tiled_kernel (csrc/MatrixExpSmall.cuh:177-385) -- one CTA
+// per padded 16x16 / 32x32 matrix with 2-8 elements per thread, operands restaged through
+// shared memory with two __syncthreads per product, fixed degree 18.
 #pragma once
 
 #include "expm_common.cuh"
 
 namespace fhx {
 
-template <int P, bool Pair>
-struct TeamCfg {
-  static constexpr int TM = 4;
-  static constexpr int TN = 8;
-  static constexpr int RB = P / TM;
-  static constexpr int CB = P / TN;
-  static constexpr int T = RB * CB;  // lanes per matrix
-  static constexpr int TPW = 32 / T;  // matrices per warp
-  static constexpr int PLANE = P * P;
-  static constexpr int SLOT = (Pair ? 2 : 1) * PLANE;
-  static constexpr int NSLOT = 4;
-  // Team regions are skewed so that teams of one warp start in different banks.
-  static constexpr int SKEW = P == 8 ? 8 : P == 16 ? 16 : 0;
-  static constexpr int TEAM_FLOATS = NSLOT * SLOT + SKEW;
-  static constexpr int WARP_FLOATS = TPW * TEAM_FLOATS;
-  static_assert(TPW * T == 32, "team size must divide the warp");
+constexpr int kSlots = 5;
+
+// Layout flags of a launch (computed on the host from strides, dtype and alignment).
+enum : unsigned {
+  kARows = 1u,    // input: consecutive elements of a row are closest in memory (s2 <= s1)
+  kAVec = 2u,     // input: float32, row-contiguous, n == P, 16-byte aligned rows
+  kERows = 4u,    // direction: as kARows
+  kEVec = 8u,     // direction: as kAVec
+  kOutVec = 16u,  // output: n % 4 == 0 and 16-byte (float32) / 8-byte (half types) aligned
+};
+constexpr int kMaxIn = 4;
+constexpr int kMaxOut = 5;
+
+// One step of a degree program: R = slot[x] * slot[y] (+ slot[z] if z >= 0), R -> slot[r],
+// then nout outputs out[o] = coef[o][0] * I + sum_j coef[o][1 + j] * slot[in[j]], evaluated
+// element-wise on the lane's own tile with every input read before any output is written.
+struct Step {
+  signed char x, y, z, r;
+  signed char nin, nout;
+  signed char in[kMaxIn];
+  signed char out[kMaxOut];
+  float coef[kMaxOut][kMaxIn + 1];
 };
 
-// Offset of element (i, j) inside a plane.
+// Programs for m = 2, 4, 8, 12, 18 (steps numbered from 0; the result ends in slot 0).
+// Slots: 0 holds A on entry.  Coefficients: BBC 2019 schemes, expm_coeffs.h.
+__constant__ Step kSteps[15] = {
+    // m = 2: A2 -> s1; s0 = I + A + A2/2
+    {0, 0, -1, 1, 2, 1, {0, 1}, {0}, {{1.f, 1.f, 0.5f}}},
+    // m = 4: A2 -> s1; s2 = I/2 + A/6 + A2/24, s3 = I + A
+    {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.5f, 1.f / 6.f, 1.f / 24.f}, {1.f, 1.f, 0.f}}},
+    //         s0 = A2 * s2 + s3
+    {1, 2, 3, 0, 0, 0, {}, {}, {}},
+    // m = 8: A2 -> s1; s2 = x1 A + x2 A2 (C1), s3 = I + A + y2 A2 (F)
+    {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.f, kT8X1, kT8X2}, {1.f, 1.f, kT8Y2}}},
+    //         A4 = A2 * C1 -> s4; s2 = x3 A2 + A4 (L), s0 = x4 I + x5 A + x6 A2 + x7 A4 (R)
+    {1, 2, -1, 4, 3, 2, {0, 1, 4}, {2, 0}, {{0.f, 0.f, kT8X3, 1.f}, {kT8X4, kT8X5, kT8X6, kT8X7}}},
+    //         s0 = L * R + F
+    {2, 0, 3, 0, 0, 0, {}, {}, {}},
+    // m = 12: A2 -> s1
+    {0, 0, -1, 1, 0, 0, {}, {}, {}},
+    //          A3 -> s2; s3 = B4, s4 = B3, s1 = B2, s0 = B1 (on I, A, A2, A3)
+    {1, 0, -1, 2, 3, 4, {0, 1, 2}, {3, 4, 1, 0},
+     {{t12c(3, 0), t12c(3, 1), t12c(3, 2), t12c(3, 3)},
+      {t12c(2, 0), t12c(2, 1), t12c(2, 2), t12c(2, 3)},
+      {t12c(1, 0), t12c(1, 1), t12c(1, 2), t12c(1, 3)},
+      {t12c(0, 0), t12c(0, 1), t12c(0, 2), t12c(0, 3)}}},
+    //          A6 = B4 * B4 + B3 -> s2; s1 = B2 + A6
+    {3, 3, 4, 2, 2, 1, {1, 2}, {1}, {{0.f, 1.f, 1.f}}},
+    //          s0 = (B2 + A6) * A6 + B1
+    {1, 2, 0, 0, 0, 0, {}, {}, {}},
+    // m = 18: A2 -> s1
+    {0, 0, -1, 1, 0, 0, {}, {}, {}},
+    //          A3 -> s2
+    {1, 0, -1, 2, 0, 0, {}, {}, {}},
+    //          A6 -> s3; s0 = B1, s1 = B5, s2 = B4, s3 = B3 + B4, s4 = B2 (on I, A, A2, A3, A6)
+    {2, 2, -1, 3, 4, 5, {0, 1, 2, 3}, {0, 1, 2, 3, 4},
+     {{t18c(0, 0), t18c(0, 1), t18c(0, 2), t18c(0, 3), t18c(0, 4)},
+      {t18c(4, 0), t18c(4, 1), t18c(4, 2), t18c(4, 3), t18c(4, 4)},
+      {t18c(3, 0), t18c(3, 1), t18c(3, 2), t18c(3, 3), t18c(3, 4)},
+      {t18c(2, 0) + t18c(3, 0), t18c(2, 1) + t18c(3, 1), t18c(2, 2) + t18c(3, 2), t18c(2, 3) + t18c(3, 3),
+       t18c(2, 4) + t18c(3, 4)},
+      {t18c(1, 0), t18c(1, 1), t18c(1, 2), t18c(1, 3), t18c(1, 4)}}},
+    //          P = B1 * B5 -> s0; s1 = P + B4 (A9), s0 = P + B3 + B4
+    {0, 1, -1, 0, 3, 2, {0, 2, 3}, {1, 0}, {{0.f, 1.f, 1.f, 0.f}, {0.f, 1.f, 0.f, 1.f}}},
+    //          s0 = (B3 + A9) * A9 + B2
+    {0, 1, 4, 0, 0, 0, {}, {}, {}},
+};
+
+__host__ __device__ __forceinline__ int program_offset(int m) {
+  return m == 2 ? 0 : m == 4 ? 1 : m == 8 ? 3 : m == 12 ? 6 : 10;
+}
+
+
+template <int P, int TN, bool Pair>
+struct TeamCfg {
+  static constexpr int RB = P / 4;
+  static constexpr int CB = P / TN;
+  static constexpr int T = RB * CB;  // threads per matrix
+  static constexpr int PLANE = P * P;
+  static constexpr int NPART = Pair ? 2 : 1;
+  static constexpr int SLOT = NPART * PLANE;
+  // Teams that share a warp start in different banks; 4 floats of per-team scratch.
+  static constexpr int SKEW = T >= 32 ? 0 : P == 8 ? 8 : 16;
+  static constexpr int TEAM_FLOATS = kSlots * SLOT + 4 + (SKEW ? SKEW - 4 : 12);
+  static_assert(T == 64 || 32 % T == 0, "team must divide a warp or be two warps");
+  static_assert(TEAM_FLOATS % 4 == 0, "16-byte aligned team regions");
+};
+
+// Offset of element (i, j) inside a plane: 16-byte chunk (j / 4) of row i is stored at
+// chunk position (j / 4) ^ (i / 4).
 template <int P>
 __device__ __forceinline__ int pidx(int i, int j) {
   return i * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
 }
 
-template <bool Pair>
-struct Tile {
-  float d[4][8];
-  float u[Pair ? 4 : 1][Pair ? 8 : 1];
+template <int T>
+__device__ __forceinline__ void team_sync(int team_in_cta) {
+  if constexpr (T <= 32) {
+    __syncwarp();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + team_in_cta), "r"(T) : "memory");
+  }
+}
+
+template <int TN, bool Pair>
+struct Acc {
+  float d[4][TN];
+  float u[Pair ? 4 : 1][Pair ? TN : 1];
 };
 
-template <bool Pair>
-__device__ __forceinline__ void tile_zero(Tile<Pair>& t) {
+template <int TN, bool Pair>
+__device__ __forceinline__ void acc_zero(Acc<TN, Pair>& R) {
 #pragma unroll
   for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      t.d[ii][jj] = 0.f;
-      if constexpr (Pair) t.u[ii][jj] = 0.f;
+    for (int jj = 0; jj < TN; ++jj) {
+      R.d[ii][jj] = 0.f;
+      if constexpr (Pair) R.u[ii][jj] = 0.f;
     }
 }
 
-// R = X Y (+ Z): X and Y point at the first (value) plane of a slot; the derivative
-// plane follows at +PLANE.
-template <int P, bool Pair>
-__device__ __forceinline__ void team_product(const float* __restrict__ X, const float* __restrict__ Y, int i0,
-                                             int j0, Tile<Pair>& R, const Tile<Pair>& Z, bool use_z) {
-  constexpr int PLANE = P * P;
-  if (use_z) {
-    R = Z;
-  } else {
-    tile_zero(R);
-  }
-#pragma unroll 4
-  for (int k = 0; k < P; ++k) {
-    float x[4], xu[4];
+// Thread-own tile <-> slot.  Own chunks: rows i0..i0+3, chunks j0/4 .. j0/4 + TN/4 - 1.
+template <int P, int TN, bool Pair>
+__device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int j0, const Acc<TN, Pair>& R) {
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      x[ii] = X[pidx<P>(i0 + ii, k)];
-      if constexpr (Pair) xu[ii] = X[PLANE + pidx<P>(i0 + ii, k)];
+  for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+    for (int c = 0; c < TN / 4; ++c) {
+      const int o = pidx<P>(i0 + ii, j0 + 4 * c);
+      *reinterpret_cast<float4*>(slot + o) =
+          make_float4(R.d[ii][4 * c], R.d[ii][4 * c + 1], R.d[ii][4 * c + 2], R.d[ii][4 * c + 3]);
+      if constexpr (Pair)
+        *reinterpret_cast<float4*>(slot + P * P + o) =
+            make_float4(R.u[ii][4 * c], R.u[ii][4 * c + 1], R.u[ii][4 * c + 2], R.u[ii][4 * c + 3]);
     }
-    float y[8], yu[8];
-    {
-      const float4 v0 = *reinterpret_cast<const float4*>(Y + pidx<P>(k, j0));
-      const float4 v1 = *reinterpret_cast<const float4*>(Y + pidx<P>(k, j0 + 4));
-      y[0] = v0.x; y[1] = v0.y; y[2] = v0.z; y[3] = v0.w;
-      y[4] = v1.x; y[5] = v1.y; y[6] = v1.z; y[7] = v1.w;
+}
+
+template <int P, int TN, bool Pair>
+__device__ __forceinline__ void acc_load(const float* __restrict__ slot, int i0, int j0, Acc<TN, Pair>& R) {
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+    for (int c = 0; c < TN / 4; ++c) {
+      const int o = pidx<P>(i0 + ii, j0 + 4 * c);
+      const float4 a = *reinterpret_cast<const float4*>(slot + o);
+      R.d[ii][4 * c] = a.x; R.d[ii][4 * c + 1] = a.y; R.d[ii][4 * c + 2] = a.z; R.d[ii][4 * c + 3] = a.w;
       if constexpr (Pair) {
-        const float4 w0 = *reinterpret_cast<const float4*>(Y + PLANE + pidx<P>(k, j0));
-        const float4 w1 = *reinterpret_cast<const float4*>(Y + PLANE + pidx<P>(k, j0 + 4));
-        yu[0] = w0.x; yu[1] = w0.y; yu[2] = w0.z; yu[3] = w0.w;
-        yu[4] = w1.x; yu[5] = w1.y; yu[6] = w1.z; yu[7] = w1.w;
+        const float4 b = *reinterpret_cast<const float4*>(slot + P * P + o);
+        R.u[ii][4 * c] = b.x; R.u[ii][4 * c + 1] = b.y; R.u[ii][4 * c + 2] = b.z; R.u[ii][4 * c + 3] = b.w;
       }
     }
+}
+
+__device__ __forceinline__ float f4get(const float4& v, int r) { return r == 0 ? v.x : r == 1 ? v.y : r == 2 ? v.z : v.w; }
+
+// R += X Y.  X, Y: first (value) plane of a slot; the derivative plane follows at +PLANE.
+template <int P, int TN, bool Pair>
+__device__ __forceinline__ void team_product(const float* __restrict__ X, const float* __restrict__ Y, int i0, int j0,
+                                             Acc<TN, Pair>& R) {
+  constexpr int PLANE = P * P;
+  constexpr int MASK = P / 4 - 1;
+  const int rb = i0 >> 2;
+  const int c0 = j0 >> 2;
+  const float* xrow = X + i0 * P;
+  // Frechet: R.u accumulates X dY, V accumulates dX Y (independent FMA chains).
+  float V[Pair ? 4 : 1][Pair ? TN : 1];
+  if constexpr (Pair) {
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        R.d[ii][jj] = fmaf(x[ii], y[jj], R.d[ii][jj]);
+      for (int jj = 0; jj < TN; ++jj) V[ii][jj] = 0.f;
+  }
+#pragma unroll 2
+  for (int q = 0; q < P / 4; ++q) {
+    const int xc = ((q ^ rb) & MASK) << 2;
+    float4 xb[4], xub[4];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      xb[ii] = *reinterpret_cast<const float4*>(xrow + ii * P + xc);
+      if constexpr (Pair) xub[ii] = *reinterpret_cast<const float4*>(xrow + PLANE + ii * P + xc);
+    }
+    const float* yrow = Y + (4 * q) * P;
+    int yc[TN / 4];
+#pragma unroll
+    for (int c = 0; c < TN / 4; ++c) yc[c] = (((c0 + c) ^ q) & MASK) << 2;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float y[TN], yu[TN];
+#pragma unroll
+      for (int c = 0; c < TN / 4; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(yrow + r * P + yc[c]);
+        y[4 * c] = v.x; y[4 * c + 1] = v.y; y[4 * c + 2] = v.z; y[4 * c + 3] = v.w;
         if constexpr (Pair) {
-          R.u[ii][jj] = fmaf(x[ii], yu[jj], R.u[ii][jj]);
-          R.u[ii][jj] = fmaf(xu[ii], y[jj], R.u[ii][jj]);
+          const float4 w = *reinterpret_cast<const float4*>(yrow + PLANE + r * P + yc[c]);
+          yu[4 * c] = w.x; yu[4 * c + 1] = w.y; yu[4 * c + 2] = w.z; yu[4 * c + 3] = w.w;
         }
       }
-  }
-}
-
-// Operands of step `st` of the degree-m program: product slots and whether Z is added.
-__device__ __forceinline__ void step_operands(int m, int st, int* xs, int* ys, bool* use_z) {
-  *xs = 0;
-  *ys = 0;
-  *use_z = false;
-  if (m == 4) {
-    if (st == 1) { *xs = 2; *ys = 1; *use_z = true; }
-  } else if (m == 8) {
-    if (st == 1) { *xs = 2; *ys = 1; }
-    else if (st == 2) { *xs = 3; *ys = 1; *use_z = true; }
-  } else if (m == 12) {
-    if (st == 1) { *xs = 1; *ys = 0; }
-    else if (st == 2) { *xs = 2; *ys = 2; *use_z = true; }
-    else if (st == 3) { *xs = 1; *ys = 2; *use_z = true; }
-  } else if (m == 18) {
-    if (st == 1) { *xs = 1; *ys = 0; }
-    else if (st == 2) { *xs = 2; *ys = 2; }
-    else if (st == 3) { *xs = 0; *ys = 1; }
-    else if (st == 4) { *xs = 0; *ys = 1; *use_z = true; }
-  }
-}
-
-// Lane-local epilogue of polynomial step `st`: reads the lane's own elements of the slots
-// and of R, writes the lane's own elements of the next operands.  `part` 0 is the value
-// plane (identity terms apply), part 1 the derivative plane.
-template <int P, bool Pair>
-__device__ __forceinline__ void step_epilogue(int m, int st, float* __restrict__ team, int i0, int j0,
-                                              Tile<Pair>& R, Tile<Pair>& Z) {
-  constexpr int PLANE = P * P;
-  constexpr int SLOT = TeamCfg<P, Pair>::SLOT;
-  constexpr int NPART = Pair ? 2 : 1;
-#pragma unroll
-  for (int part = 0; part < NPART; ++part) {
-    float* s0 = team + 0 * SLOT + part * PLANE;
-    float* s1 = team + 1 * SLOT + part * PLANE;
-    float* s2 = team + 2 * SLOT + part * PLANE;
-    float* s3 = team + 3 * SLOT + part * PLANE;
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int i = i0 + ii, j = j0 + jj;
-        const int o = pidx<P>(i, j);
-        const float id = (part == 0 && i == j) ? 1.f : 0.f;
-        float& r = (part == 0) ? R.d[ii][jj] : R.u[Pair ? ii : 0][Pair ? jj : 0];
-        float& z = (part == 0) ? Z.d[ii][jj] : Z.u[Pair ? ii : 0][Pair ? jj : 0];
-        if (m == 2) {
-          // T2 = I + A + A2 / 2
-          r = id + s0[o] + 0.5f * r;
-        } else if (m == 4) {
-          if (st == 0) {
-            const float a = s0[o], a2 = r;
-            s1[o] = 0.5f * id + a * (1.f / 6.f) + a2 * (1.f / 24.f);
-            s2[o] = a2;
-            z = id + a;
-          }
-        } else if (m == 8) {
-          if (st == 0) {
-            const float a = s0[o], a2 = r;
-            s1[o] = fmaf(kT8X1, a, kT8X2 * a2);
-            s2[o] = a2;
-            z = id + a + kT8Y2 * a2;
-          } else if (st == 1) {
-            const float a = s0[o], a2 = s2[o], a4 = r;
-            s3[o] = fmaf(kT8X3, a2, a4);
-            s1[o] = kT8X4 * id + kT8X5 * a + kT8X6 * a2 + kT8X7 * a4;
-          }
-        } else if (m == 12) {
-          if (st == 0) {
-            s1[o] = r;
-          } else if (st == 1) {
-            const float a = s0[o], a2 = s1[o], a3 = r;
-            s2[o] = t12c(3, 0) * id + t12c(3, 1) * a + t12c(3, 2) * a2 + t12c(3, 3) * a3;
-            z = t12c(2, 0) * id + t12c(2, 1) * a + t12c(2, 2) * a2 + t12c(2, 3) * a3;
-            s3[o] = t12c(1, 0) * id + t12c(1, 1) * a + t12c(1, 2) * a2 + t12c(1, 3) * a3;
-            s0[o] = t12c(0, 0) * id + t12c(0, 1) * a + t12c(0, 2) * a2 + t12c(0, 3) * a3;
-          } else if (st == 2) {
-            const float a6 = r;
-            s1[o] = s3[o] + a6;
-            s2[o] = a6;
-            z = s0[o];
-          }
-        } else {  // m == 18
-          if (st == 0) {
-            s1[o] = r;
-          } else if (st == 1) {
-            s2[o] = r;
-          } else if (st == 2) {
-            const float a = s0[o], a2 = s1[o], a3 = s2[o], a6 = r;
-            const float b1 = t18c(0, 0) * id + t18c(0, 1) * a + t18c(0, 2) * a2 + t18c(0, 3) * a3 + t18c(0, 4) * a6;
-            const float b2 = t18c(1, 0) * id + t18c(1, 1) * a + t18c(1, 2) * a2 + t18c(1, 3) * a3 + t18c(1, 4) * a6;
-            const float b3 = t18c(2, 0) * id + t18c(2, 1) * a + t18c(2, 2) * a2 + t18c(2, 3) * a3 + t18c(2, 4) * a6;
-            const float b4 = t18c(3, 0) * id + t18c(3, 1) * a + t18c(3, 2) * a2 + t18c(3, 3) * a3 + t18c(3, 4) * a6;
-            const float b5 = t18c(4, 0) * id + t18c(4, 1) * a + t18c(4, 2) * a2 + t18c(4, 3) * a3 + t18c(4, 4) * a6;
-            s0[o] = b1;
-            s1[o] = b5;
-            s2[o] = b4;
-            s3[o] = b3 + b4;
-            z = b2;
-          } else if (st == 3) {
-            const float p = r;
-            s1[o] = p + s2[o];  // A9 = B1 B5 + B4
-            s0[o] = p + s3[o];  // B3 + A9
-          }
-        }
-      }
-    }
-  }
-}
-
-template <int P, bool Pair>
-__device__ __forceinline__ void tile_to_slot(float* __restrict__ slot, int i0, int j0, const Tile<Pair>& R) {
-#pragma unroll
-  for (int ii = 0; ii < 4; ++ii) {
-    float4* p0 = reinterpret_cast<float4*>(slot + pidx<P>(i0 + ii, j0));
-    float4* p1 = reinterpret_cast<float4*>(slot + pidx<P>(i0 + ii, j0 + 4));
-    *p0 = make_float4(R.d[ii][0], R.d[ii][1], R.d[ii][2], R.d[ii][3]);
-    *p1 = make_float4(R.d[ii][4], R.d[ii][5], R.d[ii][6], R.d[ii][7]);
-    if constexpr (Pair) {
-      float4* q0 = reinterpret_cast<float4*>(slot + P * P + pidx<P>(i0 + ii, j0));
-      float4* q1 = reinterpret_cast<float4*>(slot + P * P + pidx<P>(i0 + ii, j0 + 4));
-      *q0 = make_float4(R.u[ii][0], R.u[ii][1], R.u[ii][2], R.u[ii][3]);
-      *q1 = make_float4(R.u[ii][4], R.u[ii][5], R.u[ii][6], R.u[ii][7]);
-    }
-  }
-}
-
-template <int P, bool Pair, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) expm_team_kernel(View a, View e, void* __restrict__ out,
-                                                                  int64_t batch, int n, int dtype) {
-  using C = TeamCfg<P, Pair>;
-  extern __shared__ __align__(16) float smem[];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int team_id = lane / C::T;
-  const int t = lane % C::T;
-  const int rb = t / C::CB, cb = t % C::CB;
-  const int i0 = 4 * rb, j0 = 8 * cb;
-  float* team = smem + warp * C::WARP_FLOATS + team_id * C::TEAM_FLOATS;
-  const unsigned team_mask = (C::T == 32) ? 0xffffffffu : (((1u << C::T) - 1u) << (team_id * C::T));
-
-  const int64_t n_items = (batch + C::TPW - 1) / C::TPW;
-  const int64_t warps_total = int64_t(gridDim.x) * WARPS;
-  for (int64_t item = int64_t(blockIdx.x) * WARPS + warp; item < n_items; item += warps_total) {
-    const int64_t b = item * C::TPW + team_id;
-    const bool valid = b < batch;
-
-    // ---- load the lane's tile of A (and E), zero-padded to P x P ----
-    Tile<Pair> R, Z;
-    bool bad = false;
-    double col[8], row[4];
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) col[jj] = 0.0;
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) row[ii] = 0.0;
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int i = i0 + ii, j = j0 + jj;
-        float v = 0.f, w = 0.f;
-        if (valid && i < n && j < n) {
-          v = a.sign * load_elem(a.data, dtype, b * a.s0 + i * a.s1 + j * a.s2);
-          if constexpr (Pair) w = e.sign * load_elem(e.data, dtype, b * e.s0 + i * e.s1 + j * e.s2);
-        }
-        bad |= !isfinite(v);
-        if constexpr (Pair) bad |= !isfinite(w);
-        const double av = fabs(double(v));
-        col[jj] += av;
-        row[ii] += av;
-        R.d[ii][jj] = v;
-        if constexpr (Pair) R.u[ii][jj] = w;
-      }
-    }
-    const bool team_bad = (__ballot_sync(0xffffffffu, bad) & team_mask) != 0u;
-    // Column sums over the row blocks of the team, then the largest column.
-#pragma unroll
-    for (int off = C::CB; off < C::T; off <<= 1)
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) col[jj] += __shfl_xor_sync(0xffffffffu, col[jj], off);
-#pragma unroll
-    for (int off = 1; off < C::CB; off <<= 1)
-#pragma unroll
-      for (int ii = 0; ii < 4; ++ii) row[ii] += __shfl_xor_sync(0xffffffffu, row[ii], off);
-    double n1 = 0.0, ninf = 0.0;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) n1 = fmax(n1, col[jj]);
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) ninf = fmax(ninf, row[ii]);
-#pragma unroll
-    for (int off = 1; off < C::T; off <<= 1) {
-      n1 = fmax(n1, __shfl_xor_sync(0xffffffffu, n1, off));
-      ninf = fmax(ninf, __shfl_xor_sync(0xffffffffu, ninf, off));
-    }
-    int m = 1, s = 0;
-    choose_degree(fmin(n1, ninf), &m, &s);
-    const int poly = scheme_products(m);
-    const int nsteps = (valid && !team_bad) ? poly + s : 0;
-
-    // ---- scale by 2^-s and place A in slot 0 ----
-    if (s > 0) {
-#pragma unroll
-      for (int ii = 0; ii < 4; ++ii)
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          R.d[ii][jj] = scale_pow2(R.d[ii][jj], s);
-          if constexpr (Pair) R.u[ii][jj] = scale_pow2(R.u[ii][jj], s);
-        }
-    }
-    tile_to_slot<P, Pair>(team, i0, j0, R);
-    if (m == 1) {  // T1 = I + A (s == 0 here)
-#pragma unroll
-      for (int ii = 0; ii < 4; ++ii)
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) R.d[ii][jj] += (i0 + ii == j0 + jj) ? 1.f : 0.f;
-    }
-    tile_zero(Z);
-    __syncwarp();
-
-    // ---- polynomial steps, then squarings, in lockstep across the warp ----
-    const int max_steps = __reduce_max_sync(0xffffffffu, nsteps);
-    for (int st = 0; st < max_steps; ++st) {
-      const bool active = st < nsteps;
-      int xs = 0, ys = 0;
-      bool use_z = false;
-      if (st < poly) step_operands(m, st, &xs, &ys, &use_z);
-      if (active) team_product<P, Pair>(team + xs * C::SLOT, team + ys * C::SLOT, i0, j0, R, Z, use_z);
-      __syncwarp();
-      if (active) {
-        const bool last = st == nsteps - 1;
-        if (st < poly) step_epilogue<P, Pair>(m, st, team, i0, j0, R, Z);
-        if ((st >= poly - 1) && !last) tile_to_slot<P, Pair>(team, i0, j0, R);
-      }
-      __syncwarp();
-    }
-
-    // ---- store the n x n corner ----
-    if (valid) {
-      const int64_t obase = b * int64_t(n) * n;
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii) {
+        const float x = f4get(xb[ii], r);
+        float xu = 0.f;
+        if constexpr (Pair) xu = f4get(xub[ii], r);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int i = i0 + ii, j = j0 + jj;
-          if (i < n && j < n) {
-            float v;
-            if constexpr (Pair) {
-              v = R.u[ii][jj];
-            } else {
-              v = R.d[ii][jj];
-            }
-            if (team_bad) v = __int_as_float(0x7fc00000);
-            store_elem(out, dtype, obase + int64_t(i) * n + j, v);
+        for (int jj = 0; jj < TN; ++jj) {
+          R.d[ii][jj] = fmaf(x, y[jj], R.d[ii][jj]);
+          if constexpr (Pair) {
+            R.u[ii][jj] = fmaf(x, yu[jj], R.u[ii][jj]);
+            V[ii][jj] = fmaf(xu, y[jj], V[ii][jj]);
           }
         }
       }
     }
+  }
+  if constexpr (Pair) {
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+      for (int jj = 0; jj < TN; ++jj) R.u[ii][jj] += V[ii][jj];
+  }
+}
+
+// Element-wise linear combinations of a step on the thread's own 4 x TN tile (TN 16-byte
+// chunks per plane).  Kept as a rolled loop: this is the cold part of a step.
+template <int P, int TN, bool Pair>
+__device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+  constexpr int PLANE = P * P;
+  constexpr int SLOT = TeamCfg<P, TN, Pair>::SLOT;
+  const Step& st = kSteps[step_index];
+  const int nin = st.nin, nout = st.nout;
+  float coef[kMaxOut][kMaxIn + 1];
+  int in_off[kMaxIn], out_off[kMaxOut];
+#pragma unroll
+  for (int o = 0; o < kMaxOut; ++o) {
+    out_off[o] = st.out[o] * SLOT;
+#pragma unroll
+    for (int t = 0; t < kMaxIn + 1; ++t) coef[o][t] = st.coef[o][t];
+  }
+#pragma unroll
+  for (int t = 0; t < kMaxIn; ++t) in_off[t] = st.in[t] * SLOT;
+#pragma unroll 1
+  for (int part = 0; part < (Pair ? 2 : 1); ++part) {
+#pragma unroll 2
+    for (int c = 0; c < TN; ++c) {
+      const int i = i0 + c / (TN / 4);
+      const int j = j0 + 4 * (c % (TN / 4));
+      const int off = part * PLANE + pidx<P>(i, j);
+      const int dj = part == 0 ? i - j : -1;  // identity pattern of this chunk (value plane only)
+      const float4 id = make_float4(dj == 0 ? 1.f : 0.f, dj == 1 ? 1.f : 0.f, dj == 2 ? 1.f : 0.f, dj == 3 ? 1.f : 0.f);
+      float4 in[kMaxIn];
+#pragma unroll
+      for (int t = 0; t < kMaxIn; ++t)
+        if (t < nin) in[t] = *reinterpret_cast<const float4*>(team + in_off[t] + off);
+#pragma unroll
+      for (int o = 0; o < kMaxOut; ++o) {
+        if (o < nout) {
+          const float c0 = coef[o][0];
+          float4 v = make_float4(c0 * id.x, c0 * id.y, c0 * id.z, c0 * id.w);
+#pragma unroll
+          for (int t = 0; t < kMaxIn; ++t) {
+            if (t < nin) {
+              const float cf = coef[o][1 + t];
+              v.x = fmaf(cf, in[t].x, v.x);
+              v.y = fmaf(cf, in[t].y, v.y);
+              v.z = fmaf(cf, in[t].z, v.z);
+              v.w = fmaf(cf, in[t].w, v.w);
+            }
+          }
+          *reinterpret_cast<float4*>(team + out_off[o] + off) = v;
+        }
+      }
+    }
+  }
+}
+
+// Raw bits of four consecutive elements (r, c..c+3) of matrix b of a view (zero outside the
+// n x n matrix): float32 bits, or a 16-bit value in the low half of each word.  Nothing is
+// computed from the loaded values here, so a prefetch never waits for its own loads;
+// decode_chunk converts at the point of use.  `vec`: row-contiguous float32 view with
+// 16-byte aligned rows and n == P.
+__device__ __forceinline__ uint4 load_chunk_raw(const View& v, int dtype, int64_t b, int r, int c, int n, bool vec) {
+  if (vec) {
+    const float4 x = ld_f32x4(static_cast<const float*>(v.data) + b * v.s0 + int64_t(r) * v.s1 + c);
+    return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
+  }
+  unsigned w[4];
+  const int64_t base = b * v.s0 + int64_t(r) * v.s1;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    w[u] = 0u;
+    if (r < n && c + u < n) {
+      const int64_t off = base + int64_t(c + u) * v.s2;
+      w[u] = dtype == kF32 ? __float_as_uint(ld_f32(static_cast<const float*>(v.data) + off))
+                           : unsigned(ld_u16(static_cast<const unsigned short*>(v.data) + off));
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ float decode_elem(unsigned w, int dtype, float sign) {
+  if (dtype == kF32) return sign * __uint_as_float(w);
+  const unsigned short h = static_cast<unsigned short>(w);
+  return sign * (dtype == kBF16 ? __bfloat162float(__ushort_as_bfloat16(h)) : __half2float(__ushort_as_half(h)));
+}
+
+__device__ __forceinline__ float4 decode_chunk(const uint4& w, int dtype, float sign) {
+  return make_float4(decode_elem(w.x, dtype, sign), decode_elem(w.y, dtype, sign), decode_elem(w.z, dtype, sign),
+                     decode_elem(w.w, dtype, sign));
+}
+
+__device__ __forceinline__ bool finite4(const float4& x) {
+  return isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w);
+}
+
+// Resident CTAs per SM the shared-memory footprint allows; passed to __launch_bounds__ so
+// that register allocation does not become the tighter limit.
+template <int P, int TN, bool Pair, int WARPS>
+constexpr int team_min_blocks() {
+  constexpr int smem = (WARPS * 32 / TeamCfg<P, TN, Pair>::T) * TeamCfg<P, TN, Pair>::TEAM_FLOATS * 4 + 1024;
+  // Only whole-warp teams get the bound; small teams keep their prefetch registers.
+  if constexpr (TeamCfg<P, TN, Pair>::T < 32) return 1;
+  return (228 * 1024) / smem > 16 ? 16 : (228 * 1024) / smem;
+}
+
+template <int P, int TN, bool Pair, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
+                                                                  int64_t batch, int n, int dtype, unsigned flags) {
+  const bool a_rows = flags & kARows, a_vec = flags & kAVec;
+  const bool e_rows = flags & kERows, e_vec = flags & kEVec;
+  const bool out_vec = flags & kOutVec;
+  using C = TeamCfg<P, TN, Pair>;
+  constexpr int T = C::T;
+  constexpr int TPC = WARPS * 32 / T;  // teams per CTA
+  static_assert(TPC >= 1, "CTA too small for one team");
+  extern __shared__ __align__(16) float smem[];
+  const int tic = threadIdx.x / T;  // team index in the CTA
+  const int t = threadIdx.x % T;
+  const int rb = t / C::CB, cb = t % C::CB;
+  const int i0 = 4 * rb, j0 = TN * cb;
+  float* team = smem + tic * C::TEAM_FLOATS;
+  int* scratch = reinterpret_cast<int*>(team + kSlots * C::SLOT);
+  if (t == 0) scratch[3] = 0;
+  __syncthreads();
+
+  // Every thread moves 16-byte chunks of A (and E); chunks are enumerated row-major for
+  // row-contiguous views and column-major otherwise, so that consecutive threads read
+  // consecutive addresses.
+  constexpr int CHUNKS = P * P / 4;
+  constexpr int PER_THREAD = (CHUNKS * C::NPART + T - 1) / T;
+  uint4 vals[PER_THREAD];
+  auto fetch = [&](int64_t next_item) {
+    const int64_t nb = next_item * TPC + tic;
+    const bool ok = nb < batch;
+#pragma unroll
+    for (int k = 0; k < PER_THREAD; ++k) {
+      const int idx = t + k * T;
+      const int part = idx / CHUNKS;
+      const int q = idx % CHUNKS;
+      const bool rows = part == 0 ? a_rows : e_rows;
+      const int r = rows ? q / (P / 4) : q % P;
+      const int c = rows ? 4 * (q % (P / 4)) : 4 * (q / P);
+      vals[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (ok && idx < CHUNKS * C::NPART) {
+        vals[k] = part == 0 ? load_chunk_raw(a, dtype, nb, r, c, n, a_vec) : load_chunk_raw(e, dtype, nb, r, c, n, e_vec);
+      }
+    }
+  };
+  fetch(blockIdx.x);
+  for (int64_t item = blockIdx.x; item * TPC < batch; item += gridDim.x) {
+    const int64_t b = item * TPC + tic;
+    const bool valid = b < batch;
+
+    // ---- A (and E) of this matrix, prefetched during the previous one, into slot 0 ----
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < PER_THREAD; ++k) {
+      const int idx = t + k * T;
+      if (idx < CHUNKS * C::NPART) {
+        const int part = idx / CHUNKS;
+        const int q = idx % CHUNKS;
+        const bool rows = part == 0 ? a_rows : e_rows;
+        const int r = rows ? q / (P / 4) : q % P;
+        const int c = rows ? 4 * (q % (P / 4)) : 4 * (q / P);
+        const float4 x = decode_chunk(vals[k], dtype, part == 0 ? a.sign : e.sign);
+        bad |= !finite4(x);
+        *reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P>(r, c)) = x;
+      }
+    }
+    fetch(item + gridDim.x);  // next matrix of this team: loads stay in flight during the steps
+    if (bad) scratch[3] = 1;
+    team_sync<T>(tic);
+    // ---- norms: thread t < P sums |row t| and |column t| of A in float64 ----
+    double nrow = 0.0, ncol = 0.0;
+    for (int l = t; l < P; l += T) {
+      double rs[4] = {0.0, 0.0, 0.0, 0.0}, cs[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+      for (int c4 = 0; c4 < P / 4; ++c4) {
+        const float4 x = *reinterpret_cast<const float4*>(team + pidx<P>(l, 4 * c4));
+        rs[0] += fabs(double(x.x));
+        rs[1] += fabs(double(x.y));
+        rs[2] += fabs(double(x.z));
+        rs[3] += fabs(double(x.w));
+      }
+#pragma unroll
+      for (int r = 0; r < P; ++r) cs[r & 3] += fabs(double(team[pidx<P>(r, l)]));
+      nrow = fmax(nrow, (rs[0] + rs[1]) + (rs[2] + rs[3]));
+      ncol = fmax(ncol, (cs[0] + cs[1]) + (cs[2] + cs[3]));
+    }
+    int m = 1, s = 0, nsteps = 0;
+    constexpr int RED = T < P ? T : P;  // threads 0 .. RED-1 hold norms, all in one warp
+    if (t < 32) {
+#pragma unroll
+      for (int off = 1; off < RED; off <<= 1) {
+        nrow = fmax(nrow, __shfl_xor_sync(0xffffffffu, nrow, off));
+        ncol = fmax(ncol, __shfl_xor_sync(0xffffffffu, ncol, off));
+      }
+    }
+    if constexpr (T <= 32) {
+      choose_degree(fmin(nrow, ncol), &m, &s);
+      const bool team_bad = scratch[3] != 0;
+      nsteps = (valid && !team_bad) ? scheme_products(m) + s : (team_bad ? -1 : 0);
+    } else {
+      if (t == 0) {
+        choose_degree(fmin(nrow, ncol), &m, &s);
+        const bool team_bad = scratch[3] != 0;
+        scratch[0] = m;
+        scratch[1] = s;
+        scratch[2] = (valid && !team_bad) ? scheme_products(m) + s : (team_bad ? -1 : 0);
+      }
+      team_sync<T>(tic);
+      m = scratch[0];
+      s = scratch[1];
+      nsteps = scratch[2];
+    }
+    const bool team_bad = nsteps < 0;
+    if (team_bad) nsteps = 0;
+    const int poly = scheme_products(m);
+    const int prog = program_offset(m);
+    team_sync<T>(tic);  // every column read is done before tiles are rescaled
+    if (t == 0) scratch[3] = 0;  // non-finite flag, free for the next matrix
+
+    // ---- A / 2^s (own tile), identity for the degree-1 polynomial ----
+    if (s > 0 || m == 1) {
+#pragma unroll 1
+      for (int part = 0; part < C::NPART; ++part) {
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+          for (int c = 0; c < TN / 4; ++c) {
+            float4* p = reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P>(i0 + ii, j0 + 4 * c));
+            float4 v = *p;
+            v.x = scale_pow2(v.x, s);
+            v.y = scale_pow2(v.y, s);
+            v.z = scale_pow2(v.z, s);
+            v.w = scale_pow2(v.w, s);
+            if (m == 1 && part == 0) {
+              const int dj = (i0 + ii) - (j0 + 4 * c);
+              v.x += dj == 0 ? 1.f : 0.f;
+              v.y += dj == 1 ? 1.f : 0.f;
+              v.z += dj == 2 ? 1.f : 0.f;
+              v.w += dj == 3 ? 1.f : 0.f;
+            }
+            *p = v;
+          }
+      }
+    }
+    team_sync<T>(tic);
+
+    // ---- polynomial steps, then squarings ----
+    int max_steps = nsteps;
+    if constexpr (T < 32) max_steps = __reduce_max_sync(0xffffffffu, nsteps);
+    for (int st = 0; st < max_steps; ++st) {
+      const bool active = st < nsteps;
+      const bool is_poly = st < poly;
+      const Step* step = &kSteps[prog + (is_poly ? st : 0)];
+      const int xs = is_poly ? step->x : 0;
+      const int ys = is_poly ? step->y : 0;
+      const int zs = is_poly ? step->z : -1;
+      const int rs = is_poly ? step->r : 0;
+      Acc<TN, Pair> R;
+      if (active) {
+        if (zs >= 0) {
+          acc_load<P, TN, Pair>(team + zs * C::SLOT, i0, j0, R);
+        } else {
+          acc_zero(R);
+        }
+        team_product<P, TN, Pair>(team + xs * C::SLOT, team + ys * C::SLOT, i0, j0, R);
+      }
+      team_sync<T>(tic);
+      if (active) {
+        acc_store<P, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
+        if (is_poly && step->nout > 0) team_epilogue<P, TN, Pair>(prog + st, team, i0, j0);
+      }
+      team_sync<T>(tic);
+    }
+
+    // ---- the n x n result, 16-byte chunks spread over the team ----
+    if (valid) {
+      const float* res = team + (Pair ? C::PLANE : 0);
+      const float nanv = __int_as_float(0x7fc00000);
+#pragma unroll 1
+      for (int idx = t; idx < n * (P / 4); idx += T) {
+        const int r = idx / (P / 4);
+        const int c = 4 * (idx % (P / 4));
+        if (c >= n) continue;
+        float4 v = *reinterpret_cast<const float4*>(res + pidx<P>(r, c));
+        if (team_bad) v = make_float4(nanv, nanv, nanv, nanv);
+        const int64_t o = (b * n + r) * int64_t(n) + c;
+        if (out_vec) {
+          store_chunk(out, dtype, o, v);
+        } else {
+          const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c + u < n) store_elem(out, dtype, o + u, vals[u]);
+        }
+      }
+    }
+    team_sync<T>(tic);
+    if (t == 0) scratch[3] = 0;
+    team_sync<T>(tic);
   }
 }
 

@@ -6,6 +6,7 @@
 // contiguous FP32 copy of the input (and of the direction), zero-padded to 4/8/16/32, and
 // un-pads the output with another copy; here the kernels read any strided view in the I/O
 // dtype directly and write the n x n output once.
+#include <cstdint>
 #include <mutex>
 
 #include "expm_common.cuh"
@@ -17,7 +18,6 @@ namespace fhx {
 namespace {
 
 constexpr int kMaxDevices = 64;
-constexpr int kTeamWarps = 2;
 
 struct DeviceInfo {
   bool ready = false;
@@ -67,23 +67,45 @@ int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype
   return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
 }
 
-template <int P, bool Pair>
+bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
+
+// Load/store layout flags of the team kernel (see the enum in expm_team.cuh).
+template <int P>
+unsigned layout_flags(const View& a, const View& e, const void* out, int n, int dtype, bool pair) {
+  unsigned f = 0;
+  auto vec = [&](const View& v) {
+    return dtype == kF32 && n == P && v.s2 == 1 && v.s1 % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, 16);
+  };
+  if (a.s2 <= a.s1) f |= kARows;
+  if (vec(a)) f |= kAVec;
+  if (pair) {
+    if (e.s2 <= e.s1) f |= kERows;
+    if (vec(e)) f |= kEVec;
+  }
+  const size_t esz = dtype == kF32 ? 4 : 2;
+  if (n % 4 == 0 && aligned(out, 4 * esz)) f |= kOutVec;
+  return f;
+}
+
+// TN: columns of a thread's register tile; WARPS: warps per CTA.  A team is
+// (P/4) * (P/TN) threads; one CTA holds WARPS * 32 / team-size teams.
+template <int P, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
-  using C = TeamCfg<P, Pair>;
+  using C = TeamCfg<P, TN, Pair>;
+  constexpr int threads = WARPS * 32;
+  constexpr int teams = threads / C::T;
+  constexpr size_t smem = size_t(teams) * C::TEAM_FLOATS * sizeof(float);
   static LaunchShape shape;
-  constexpr int threads = kTeamWarps * 32;
-  constexpr size_t smem = size_t(kTeamWarps) * C::WARP_FLOATS * sizeof(float);
-  auto kernel = expm_team_kernel<P, Pair, kTeamWarps>;
+  auto kernel = expm_team_kernel<P, TN, Pair, WARPS>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
   const int sms = device_sms(dev);
   const int per_sm = resident_blocks(kernel, shape, dev, threads, smem);
   if (sms <= 0 || per_sm <= 0) return FHX_ERR_CUDA;
-  const int64_t items = (batch + C::TPW - 1) / C::TPW;
-  const int64_t needed = (items + kTeamWarps - 1) / kTeamWarps;
+  const int64_t items = (batch + teams - 1) / teams;
   const int64_t resident = int64_t(sms) * per_sm;
-  const int blocks = int(needed < resident ? needed : resident);
-  kernel<<<blocks, threads, smem, stream>>>(a, e, out, batch, n, dtype);
+  const int blocks = int(items < resident ? items : resident);
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, batch, n, dtype, layout_flags<P>(a, e, out, n, dtype, Pair));
   return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
 }
 
@@ -95,9 +117,11 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
     case 4: return launch_reg<4, Pair>(a, e, out, batch, dtype, stream);
     default: break;
   }
-  if (n <= 8) return launch_team<8, Pair>(a, e, out, batch, n, dtype, stream);
-  if (n <= 16) return launch_team<16, Pair>(a, e, out, batch, n, dtype, stream);
-  return launch_team<32, Pair>(a, e, out, batch, n, dtype, stream);
+  // Frechet pairs use 4 x 4 tiles (more threads per matrix for the same shared state).
+  constexpr int TN = Pair ? 4 : 8;
+  if (n <= 8) return launch_team<8, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  if (n <= 16) return launch_team<16, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  return launch_team<32, TN, Pair, Pair ? 2 : 1>(a, e, out, batch, n, dtype, stream);
 }
 
 int check_common(int64_t batch, int32_t n, int32_t dtype, const void* out) {
