@@ -1,7 +1,7 @@
 // Team kernel: padded sizes P = 8, 16, 32 (n = 5..32).
 //
-// A "team" of T = (P/4) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
-// the 4 x TN register tile at rows 4rb.., columns TN*cb...  TN = 8 or 4 per configuration,
+// A "team" of T = (P/TM) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
+// the TM x TN register tile at rows TM*rb.., columns TN*cb...  TN = 8 or 4 per configuration,
 // so a team is 2..32 lanes of one warp or, for the 32 x 32 Frechet derivative, two warps.
 // The matrix state lives in five shared-memory plane slots per team; registers hold only
 // the accumulator tile of the product in flight.
@@ -42,11 +42,14 @@ namespace fhx {
 constexpr int kSlots = 5;
 
 // Layout flags of a launch (computed on the host from strides, dtype and alignment).
+// A view is moved in 16-byte chunks: four consecutive elements of a row ("row chunks",
+// when the elements of a row are closest in memory, s2 <= s1) or of a column ("column
+// chunks", s1 < s2).  "Vec": float32, the chunk contiguous and 16-byte aligned, n == P.
 enum : unsigned {
-  kARows = 1u,    // input: consecutive elements of a row are closest in memory (s2 <= s1)
-  kAVec = 2u,     // input: float32, row-contiguous, n == P, 16-byte aligned rows
-  kERows = 4u,    // direction: as kARows
-  kEVec = 8u,     // direction: as kAVec
+  kARows = 1u,    // input: row chunks
+  kAVec = 2u,     // input: one 128-bit load per chunk
+  kERows = 4u,    // direction: row chunks
+  kEVec = 8u,     // direction: one 128-bit load per chunk
   kOutVec = 16u,  // output: n % 4 == 0 and 16-byte (float32) / 8-byte (half types) aligned
 };
 constexpr int kMaxIn = 4;
@@ -113,9 +116,9 @@ __host__ __device__ __forceinline__ int program_offset(int m) {
 }
 
 
-template <int P, int TN, bool Pair>
+template <int P, int TM, int TN, bool Pair>
 struct TeamCfg {
-  static constexpr int RB = P / 4;
+  static constexpr int RB = P / TM;
   static constexpr int CB = P / TN;
   static constexpr int T = RB * CB;  // threads per matrix
   static constexpr int PLANE = P * P;
@@ -124,15 +127,23 @@ struct TeamCfg {
   // Teams that share a warp start in different banks; 4 floats of per-team scratch.
   static constexpr int SKEW = T >= 32 ? 0 : P == 8 ? 8 : 16;
   static constexpr int TEAM_FLOATS = kSlots * SLOT + 4 + (SKEW ? SKEW - 4 : 12);
-  static_assert(T == 64 || 32 % T == 0, "team must divide a warp or be two warps");
+  static_assert(32 % T == 0 || (T % 32 == 0 && T <= 256), "team must divide a warp or be whole warps");
+  // Thread -> tile map: each quarter-warp (8 threads) covers QR row blocks x QC column
+  // blocks.  A 128-bit shared load costs 2 wavefronts when every quarter-warp touches at
+  // most two distinct 16-byte chunks and 4 otherwise (measured), so the more frequent load
+  // (X blocks: TM per k-group, Y rows: TN per k-group) gets the quarter with <= 2 chunks.
+  static constexpr int QR = (T < 8) ? 1 : (TN >= TM ? (RB >= 4 ? 4 : RB) : 2);
+  static constexpr int QC = (T < 8) ? 1 : 8 / QR;
+  static_assert(T < 8 || (RB % QR == 0 && CB % QC == 0 && QR * QC == 8), "quarter-warp tiling");
   static_assert(TEAM_FLOATS % 4 == 0, "16-byte aligned team regions");
 };
 
 // Offset of element (i, j) inside a plane: 16-byte chunk (j / 4) of row i is stored at
-// chunk position (j / 4) ^ (i / 4).
-template <int P>
+// chunk position (j / 4) ^ (i / TM), TM the height of a thread's tile.  The TM rows of one
+// tile share a rotation; the row blocks of a warp get different ones.
+template <int P, int TM>
 __device__ __forceinline__ int pidx(int i, int j) {
-  return i * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
+  return i * P + ((((j >> 2) ^ (i / TM)) & (P / 4 - 1)) << 2) + (j & 3);
 }
 
 template <int T>
@@ -144,16 +155,16 @@ __device__ __forceinline__ void team_sync(int team_in_cta) {
   }
 }
 
-template <int TN, bool Pair>
+template <int TM, int TN, bool Pair>
 struct Acc {
-  float d[4][TN];
-  float u[Pair ? 4 : 1][Pair ? TN : 1];
+  float d[TM][TN];
+  float u[Pair ? TM : 1][Pair ? TN : 1];
 };
 
-template <int TN, bool Pair>
-__device__ __forceinline__ void acc_zero(Acc<TN, Pair>& R) {
+template <int TM, int TN, bool Pair>
+__device__ __forceinline__ void acc_zero(Acc<TM, TN, Pair>& R) {
 #pragma unroll
-  for (int ii = 0; ii < 4; ++ii)
+  for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
     for (int jj = 0; jj < TN; ++jj) {
       R.d[ii][jj] = 0.f;
@@ -162,13 +173,13 @@ __device__ __forceinline__ void acc_zero(Acc<TN, Pair>& R) {
 }
 
 // Thread-own tile <-> slot.  Own chunks: rows i0..i0+3, chunks j0/4 .. j0/4 + TN/4 - 1.
-template <int P, int TN, bool Pair>
-__device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int j0, const Acc<TN, Pair>& R) {
+template <int P, int TM, int TN, bool Pair>
+__device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int j0, const Acc<TM, TN, Pair>& R) {
 #pragma unroll
-  for (int ii = 0; ii < 4; ++ii)
+  for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
     for (int c = 0; c < TN / 4; ++c) {
-      const int o = pidx<P>(i0 + ii, j0 + 4 * c);
+      const int o = pidx<P, TM>(i0 + ii, j0 + 4 * c);
       *reinterpret_cast<float4*>(slot + o) =
           make_float4(R.d[ii][4 * c], R.d[ii][4 * c + 1], R.d[ii][4 * c + 2], R.d[ii][4 * c + 3]);
       if constexpr (Pair)
@@ -177,13 +188,13 @@ __device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int 
     }
 }
 
-template <int P, int TN, bool Pair>
-__device__ __forceinline__ void acc_load(const float* __restrict__ slot, int i0, int j0, Acc<TN, Pair>& R) {
+template <int P, int TM, int TN, bool Pair>
+__device__ __forceinline__ void acc_load(const float* __restrict__ slot, int i0, int j0, Acc<TM, TN, Pair>& R) {
 #pragma unroll
-  for (int ii = 0; ii < 4; ++ii)
+  for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
     for (int c = 0; c < TN / 4; ++c) {
-      const int o = pidx<P>(i0 + ii, j0 + 4 * c);
+      const int o = pidx<P, TM>(i0 + ii, j0 + 4 * c);
       const float4 a = *reinterpret_cast<const float4*>(slot + o);
       R.d[ii][4 * c] = a.x; R.d[ii][4 * c + 1] = a.y; R.d[ii][4 * c + 2] = a.z; R.d[ii][4 * c + 3] = a.w;
       if constexpr (Pair) {
@@ -195,50 +206,65 @@ __device__ __forceinline__ void acc_load(const float* __restrict__ slot, int i0,
 
 __device__ __forceinline__ float f4get(const float4& v, int r) { return r == 0 ? v.x : r == 1 ? v.y : r == 2 ? v.z : v.w; }
 
+// 128-bit shared-memory load from a 32-bit shared address.  Written as explicit ld.shared:
+// for the product's access pattern this costs one shared-memory wavefront per load, where the
+// compiler's own code for the same float4 dereference measured about 3.3 (ncu,
+// l1tex__data_pipe_lsu_wavefronts_mem_shared_op_ld) and saturated the shared-memory pipe.
+__device__ __forceinline__ float4 lds128(unsigned addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ unsigned smem_addr(const float* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
 // R += X Y.  X, Y: first (value) plane of a slot; the derivative plane follows at +PLANE.
-template <int P, int TN, bool Pair>
+template <int P, int TM, int TN, bool Pair>
 __device__ __forceinline__ void team_product(const float* __restrict__ X, const float* __restrict__ Y, int i0, int j0,
-                                             Acc<TN, Pair>& R) {
-  constexpr int PLANE = P * P;
+                                             Acc<TM, TN, Pair>& R) {
+  constexpr unsigned PLANE_B = P * P * 4;  // bytes
   constexpr int MASK = P / 4 - 1;
-  const int rb = i0 >> 2;
+  const int rb = i0 / TM;
   const int c0 = j0 >> 2;
-  const float* xrow = X + i0 * P;
+  const unsigned xrow = smem_addr(X) + unsigned(i0 * P) * 4u;
+  const unsigned ybase = smem_addr(Y);
   // Frechet: R.u accumulates X dY, V accumulates dX Y (independent FMA chains).
-  float V[Pair ? 4 : 1][Pair ? TN : 1];
+  float V[Pair ? TM : 1][Pair ? TN : 1];
   if constexpr (Pair) {
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii)
+    for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
       for (int jj = 0; jj < TN; ++jj) V[ii][jj] = 0.f;
   }
-#pragma unroll 2
+#pragma unroll(Pair ? 1 : 2)
   for (int q = 0; q < P / 4; ++q) {
-    const int xc = ((q ^ rb) & MASK) << 2;
-    float4 xb[4], xub[4];
+    const unsigned xc = unsigned((q ^ rb) & MASK) << 4;
+    float4 xb[TM], xub[TM];
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      xb[ii] = *reinterpret_cast<const float4*>(xrow + ii * P + xc);
-      if constexpr (Pair) xub[ii] = *reinterpret_cast<const float4*>(xrow + PLANE + ii * P + xc);
+    for (int ii = 0; ii < TM; ++ii) {
+      xb[ii] = lds128(xrow + unsigned(ii * P) * 4u + xc);
+      if constexpr (Pair) xub[ii] = lds128(xrow + PLANE_B + unsigned(ii * P) * 4u + xc);
     }
-    const float* yrow = Y + (4 * q) * P;
-    int yc[TN / 4];
-#pragma unroll
-    for (int c = 0; c < TN / 4; ++c) yc[c] = (((c0 + c) ^ q) & MASK) << 2;
+    const unsigned yrow = ybase + unsigned(4 * q * P) * 4u;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
+      // row k = 4q + r of Y is rotated by k / TM
+      const int rot = (4 * q + r) / TM;
       float y[TN], yu[TN];
 #pragma unroll
       for (int c = 0; c < TN / 4; ++c) {
-        const float4 v = *reinterpret_cast<const float4*>(yrow + r * P + yc[c]);
+        const unsigned yc = unsigned(((c0 + c) ^ rot) & MASK) << 4;
+        const float4 v = lds128(yrow + unsigned(r * P) * 4u + yc);
         y[4 * c] = v.x; y[4 * c + 1] = v.y; y[4 * c + 2] = v.z; y[4 * c + 3] = v.w;
         if constexpr (Pair) {
-          const float4 w = *reinterpret_cast<const float4*>(yrow + PLANE + r * P + yc[c]);
+          const float4 w = lds128(yrow + PLANE_B + unsigned(r * P) * 4u + yc);
           yu[4 * c] = w.x; yu[4 * c + 1] = w.y; yu[4 * c + 2] = w.z; yu[4 * c + 3] = w.w;
         }
       }
 #pragma unroll
-      for (int ii = 0; ii < 4; ++ii) {
+      for (int ii = 0; ii < TM; ++ii) {
         const float x = f4get(xb[ii], r);
         float xu = 0.f;
         if constexpr (Pair) xu = f4get(xub[ii], r);
@@ -255,7 +281,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   }
   if constexpr (Pair) {
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii)
+    for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
       for (int jj = 0; jj < TN; ++jj) R.u[ii][jj] += V[ii][jj];
   }
@@ -263,10 +289,10 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
 
 // Element-wise linear combinations of a step on the thread's own 4 x TN tile (TN 16-byte
 // chunks per plane).  Kept as a rolled loop: this is the cold part of a step.
-template <int P, int TN, bool Pair>
+template <int P, int TM, int TN, bool Pair>
 __device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
   constexpr int PLANE = P * P;
-  constexpr int SLOT = TeamCfg<P, TN, Pair>::SLOT;
+  constexpr int SLOT = TeamCfg<P, TM, TN, Pair>::SLOT;
   const Step& st = kSteps[step_index];
   const int nin = st.nin, nout = st.nout;
   float coef[kMaxOut][kMaxIn + 1];
@@ -282,10 +308,10 @@ __device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ t
 #pragma unroll 1
   for (int part = 0; part < (Pair ? 2 : 1); ++part) {
 #pragma unroll 2
-    for (int c = 0; c < TN; ++c) {
+    for (int c = 0; c < TM * TN / 4; ++c) {
       const int i = i0 + c / (TN / 4);
       const int j = j0 + 4 * (c % (TN / 4));
-      const int off = part * PLANE + pidx<P>(i, j);
+      const int off = part * PLANE + pidx<P, TM>(i, j);
       const int dj = part == 0 ? i - j : -1;  // identity pattern of this chunk (value plane only)
       const float4 id = make_float4(dj == 0 ? 1.f : 0.f, dj == 1 ? 1.f : 0.f, dj == 2 ? 1.f : 0.f, dj == 3 ? 1.f : 0.f);
       float4 in[kMaxIn];
@@ -314,28 +340,42 @@ __device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ t
   }
 }
 
-// Raw bits of four consecutive elements (r, c..c+3) of matrix b of a view (zero outside the
-// n x n matrix): float32 bits, or a 16-bit value in the low half of each word.  Nothing is
-// computed from the loaded values here, so a prefetch never waits for its own loads;
-// decode_chunk converts at the point of use.  `vec`: row-contiguous float32 view with
-// 16-byte aligned rows and n == P.
-__device__ __forceinline__ uint4 load_chunk_raw(const View& v, int dtype, int64_t b, int r, int c, int n, bool vec) {
+// Raw bits of one chunk of matrix b of a view (zero outside the n x n matrix): elements
+// (r, c..c+3) for a row chunk, (r..r+3, c) for a column chunk; float32 bits, or a 16-bit
+// value in the low half of each word.  Nothing is computed from the loaded values here, so a
+// prefetch never waits for its own loads; decode_chunk converts at the point of use.
+__device__ __forceinline__ uint4 load_chunk_raw(const View& v, int dtype, int64_t b, int r, int c, int n, bool rowc,
+                                                bool vec) {
+  const int64_t base = b * v.s0 + int64_t(r) * v.s1 + int64_t(c) * v.s2;
   if (vec) {
-    const float4 x = ld_f32x4(static_cast<const float*>(v.data) + b * v.s0 + int64_t(r) * v.s1 + c);
+    const float4 x = ld_f32x4(static_cast<const float*>(v.data) + base);
     return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
   }
+  const int64_t step = rowc ? v.s2 : v.s1;
   unsigned w[4];
-  const int64_t base = b * v.s0 + int64_t(r) * v.s1;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     w[u] = 0u;
-    if (r < n && c + u < n) {
-      const int64_t off = base + int64_t(c + u) * v.s2;
+    if ((rowc ? r : r + u) < n && (rowc ? c + u : c) < n) {
+      const int64_t off = base + u * step;
       w[u] = dtype == kF32 ? __float_as_uint(ld_f32(static_cast<const float*>(v.data) + off))
                            : unsigned(ld_u16(static_cast<const unsigned short*>(v.data) + off));
     }
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Chunk q of a P x P matrix: row chunks enumerate (row, column block) row-major, column chunks
+// (column, row block) column-major, so consecutive threads read consecutive addresses.
+template <int P>
+__device__ __forceinline__ void chunk_coords(int q, bool rowc, int* r, int* c) {
+  if (rowc) {
+    *r = q / (P / 4);
+    *c = 4 * (q % (P / 4));
+  } else {
+    *r = 4 * (q % (P / 4));
+    *c = q / (P / 4);
+  }
 }
 
 __device__ __forceinline__ float decode_elem(unsigned w, int dtype, float sign) {
@@ -355,29 +395,37 @@ __device__ __forceinline__ bool finite4(const float4& x) {
 
 // Resident CTAs per SM the shared-memory footprint allows; passed to __launch_bounds__ so
 // that register allocation does not become the tighter limit.
-template <int P, int TN, bool Pair, int WARPS>
+template <int P, int TM, int TN, bool Pair, int WARPS>
 constexpr int team_min_blocks() {
-  constexpr int smem = (WARPS * 32 / TeamCfg<P, TN, Pair>::T) * TeamCfg<P, TN, Pair>::TEAM_FLOATS * 4 + 1024;
+  constexpr int smem = (WARPS * 32 / TeamCfg<P, TM, TN, Pair>::T) * TeamCfg<P, TM, TN, Pair>::TEAM_FLOATS * 4 + 1024;
   // Only whole-warp teams get the bound; small teams keep their prefetch registers.
-  if constexpr (TeamCfg<P, TN, Pair>::T < 32) return 1;
+  if constexpr (TeamCfg<P, TM, TN, Pair>::T < 32) return 1;
   return (228 * 1024) / smem > 16 ? 16 : (228 * 1024) / smem;
 }
 
-template <int P, int TN, bool Pair, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
+template <int P, int TM, int TN, bool Pair, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
                                                                   int64_t batch, int n, int dtype, unsigned flags) {
   const bool a_rows = flags & kARows, a_vec = flags & kAVec;
   const bool e_rows = flags & kERows, e_vec = flags & kEVec;
   const bool out_vec = flags & kOutVec;
-  using C = TeamCfg<P, TN, Pair>;
+  using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int T = C::T;
   constexpr int TPC = WARPS * 32 / T;  // teams per CTA
   static_assert(TPC >= 1, "CTA too small for one team");
   extern __shared__ __align__(16) float smem[];
   const int tic = threadIdx.x / T;  // team index in the CTA
   const int t = threadIdx.x % T;
-  const int rb = t / C::CB, cb = t % C::CB;
-  const int i0 = 4 * rb, j0 = TN * cb;
+  int rb, cb;
+  if constexpr (T < 8) {
+    rb = t / C::CB;
+    cb = t % C::CB;
+  } else {
+    const int u = t / 8, v = t % 8;  // quarter-warp u, thread v within it
+    rb = (u / (C::CB / C::QC)) * C::QR + v / C::QC;
+    cb = (u % (C::CB / C::QC)) * C::QC + v % C::QC;
+  }
+  const int i0 = TM * rb, j0 = TN * cb;
   float* team = smem + tic * C::TEAM_FLOATS;
   int* scratch = reinterpret_cast<int*>(team + kSlots * C::SLOT);
   if (t == 0) scratch[3] = 0;
@@ -397,12 +445,13 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARP
       const int idx = t + k * T;
       const int part = idx / CHUNKS;
       const int q = idx % CHUNKS;
-      const bool rows = part == 0 ? a_rows : e_rows;
-      const int r = rows ? q / (P / 4) : q % P;
-      const int c = rows ? 4 * (q % (P / 4)) : 4 * (q / P);
+      const bool rowc = part == 0 ? a_rows : e_rows;
+      int r, c;
+      chunk_coords<P>(q, rowc, &r, &c);
       vals[k] = make_uint4(0u, 0u, 0u, 0u);
       if (ok && idx < CHUNKS * C::NPART) {
-        vals[k] = part == 0 ? load_chunk_raw(a, dtype, nb, r, c, n, a_vec) : load_chunk_raw(e, dtype, nb, r, c, n, e_vec);
+        vals[k] = part == 0 ? load_chunk_raw(a, dtype, nb, r, c, n, rowc, a_vec)
+                            : load_chunk_raw(e, dtype, nb, r, c, n, rowc, e_vec);
       }
     }
   };
@@ -419,33 +468,52 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARP
       if (idx < CHUNKS * C::NPART) {
         const int part = idx / CHUNKS;
         const int q = idx % CHUNKS;
-        const bool rows = part == 0 ? a_rows : e_rows;
-        const int r = rows ? q / (P / 4) : q % P;
-        const int c = rows ? 4 * (q % (P / 4)) : 4 * (q / P);
+        const bool rowc = part == 0 ? a_rows : e_rows;
+        int r, c;
+        chunk_coords<P>(q, rowc, &r, &c);
         const float4 x = decode_chunk(vals[k], dtype, part == 0 ? a.sign : e.sign);
         bad |= !finite4(x);
-        *reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P>(r, c)) = x;
+        float* plane = team + part * C::PLANE;
+        if (rowc) {
+          *reinterpret_cast<float4*>(plane + pidx<P, TM>(r, c)) = x;
+        } else {
+          plane[pidx<P, TM>(r, c)] = x.x;
+          plane[pidx<P, TM>(r + 1, c)] = x.y;
+          plane[pidx<P, TM>(r + 2, c)] = x.z;
+          plane[pidx<P, TM>(r + 3, c)] = x.w;
+        }
       }
     }
     fetch(item + gridDim.x);  // next matrix of this team: loads stay in flight during the steps
     if (bad) scratch[3] = 1;
     team_sync<T>(tic);
     // ---- norms: thread t < P sums |row t| and |column t| of A in float64 ----
+    // Sums of |a| in four float32 partial sums combined in float64; a partial sum that
+    // overflows float32 (entries near the float32 limit) is redone in float64.
     double nrow = 0.0, ncol = 0.0;
     for (int l = t; l < P; l += T) {
-      double rs[4] = {0.0, 0.0, 0.0, 0.0}, cs[4] = {0.0, 0.0, 0.0, 0.0};
+      float rs[4] = {0.f, 0.f, 0.f, 0.f}, cs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c4 = 0; c4 < P / 4; ++c4) {
-        const float4 x = *reinterpret_cast<const float4*>(team + pidx<P>(l, 4 * c4));
-        rs[0] += fabs(double(x.x));
-        rs[1] += fabs(double(x.y));
-        rs[2] += fabs(double(x.z));
-        rs[3] += fabs(double(x.w));
+        const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(l, 4 * c4));
+        rs[0] += fabsf(x.x);
+        rs[1] += fabsf(x.y);
+        rs[2] += fabsf(x.z);
+        rs[3] += fabsf(x.w);
       }
 #pragma unroll
-      for (int r = 0; r < P; ++r) cs[r & 3] += fabs(double(team[pidx<P>(r, l)]));
-      nrow = fmax(nrow, (rs[0] + rs[1]) + (rs[2] + rs[3]));
-      ncol = fmax(ncol, (cs[0] + cs[1]) + (cs[2] + cs[3]));
+      for (int r = 0; r < P; ++r) cs[r & 3] += fabsf(team[pidx<P, TM>(r, l)]);
+      double rsum = (double(rs[0]) + double(rs[1])) + (double(rs[2]) + double(rs[3]));
+      double csum = (double(cs[0]) + double(cs[1])) + (double(cs[2]) + double(cs[3]));
+      if (!isfinite(rsum) || !isfinite(csum)) {
+        rsum = csum = 0.0;
+        for (int r = 0; r < P; ++r) {
+          rsum += fabs(double(team[pidx<P, TM>(l, r)]));
+          csum += fabs(double(team[pidx<P, TM>(r, l)]));
+        }
+      }
+      nrow = fmax(nrow, rsum);
+      ncol = fmax(ncol, csum);
     }
     int m = 1, s = 0, nsteps = 0;
     constexpr int RED = T < P ? T : P;  // threads 0 .. RED-1 hold norms, all in one warp
@@ -485,10 +553,10 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARP
 #pragma unroll 1
       for (int part = 0; part < C::NPART; ++part) {
 #pragma unroll
-        for (int ii = 0; ii < 4; ++ii)
+        for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
           for (int c = 0; c < TN / 4; ++c) {
-            float4* p = reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P>(i0 + ii, j0 + 4 * c));
+            float4* p = reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P, TM>(i0 + ii, j0 + 4 * c));
             float4 v = *p;
             v.x = scale_pow2(v.x, s);
             v.y = scale_pow2(v.y, s);
@@ -518,19 +586,19 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARP
       const int ys = is_poly ? step->y : 0;
       const int zs = is_poly ? step->z : -1;
       const int rs = is_poly ? step->r : 0;
-      Acc<TN, Pair> R;
+      Acc<TM, TN, Pair> R;
       if (active) {
         if (zs >= 0) {
-          acc_load<P, TN, Pair>(team + zs * C::SLOT, i0, j0, R);
+          acc_load<P, TM, TN, Pair>(team + zs * C::SLOT, i0, j0, R);
         } else {
           acc_zero(R);
         }
-        team_product<P, TN, Pair>(team + xs * C::SLOT, team + ys * C::SLOT, i0, j0, R);
+        team_product<P, TM, TN, Pair>(team + xs * C::SLOT, team + ys * C::SLOT, i0, j0, R);
       }
       team_sync<T>(tic);
       if (active) {
-        acc_store<P, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
-        if (is_poly && step->nout > 0) team_epilogue<P, TN, Pair>(prog + st, team, i0, j0);
+        acc_store<P, TM, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
+        if (is_poly && step->nout > 0) team_epilogue<P, TM, TN, Pair>(prog + st, team, i0, j0);
       }
       team_sync<T>(tic);
     }
@@ -544,7 +612,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TN, Pair, WARP
         const int r = idx / (P / 4);
         const int c = 4 * (idx % (P / 4));
         if (c >= n) continue;
-        float4 v = *reinterpret_cast<const float4*>(res + pidx<P>(r, c));
+        float4 v = *reinterpret_cast<const float4*>(res + pidx<P, TM>(r, c));
         if (team_bad) v = make_float4(nanv, nanv, nanv, nanv);
         const int64_t o = (b * n + r) * int64_t(n) + c;
         if (out_vec) {

@@ -73,13 +73,18 @@ bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(
 template <int P>
 unsigned layout_flags(const View& a, const View& e, const void* out, int n, int dtype, bool pair) {
   unsigned f = 0;
+  // Row chunks when the elements of a row are closest in memory, else column chunks; a chunk
+  // is one 128-bit load when it is contiguous, 16-byte aligned, float32 and n == P.
+  auto rows = [](const View& v) { return v.s2 <= v.s1; };
   auto vec = [&](const View& v) {
-    return dtype == kF32 && n == P && v.s2 == 1 && v.s1 % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, 16);
+    const int64_t inner = rows(v) ? v.s2 : v.s1;
+    const int64_t outer = rows(v) ? v.s1 : v.s2;
+    return dtype == kF32 && n == P && inner == 1 && outer % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, 16);
   };
-  if (a.s2 <= a.s1) f |= kARows;
+  if (rows(a)) f |= kARows;
   if (vec(a)) f |= kAVec;
   if (pair) {
-    if (e.s2 <= e.s1) f |= kERows;
+    if (rows(e)) f |= kERows;
     if (vec(e)) f |= kEVec;
   }
   const size_t esz = dtype == kF32 ? 4 : 2;
@@ -89,14 +94,14 @@ unsigned layout_flags(const View& a, const View& e, const void* out, int n, int 
 
 // TN: columns of a thread's register tile; WARPS: warps per CTA.  A team is
 // (P/4) * (P/TN) threads; one CTA holds WARPS * 32 / team-size teams.
-template <int P, int TN, bool Pair, int WARPS>
+template <int P, int TM, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
-  using C = TeamCfg<P, TN, Pair>;
+  using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int threads = WARPS * 32;
   constexpr int teams = threads / C::T;
   constexpr size_t smem = size_t(teams) * C::TEAM_FLOATS * sizeof(float);
   static LaunchShape shape;
-  auto kernel = expm_team_kernel<P, TN, Pair, WARPS>;
+  auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
   const int sms = device_sms(dev);
@@ -117,11 +122,18 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
     case 4: return launch_reg<4, Pair>(a, e, out, batch, dtype, stream);
     default: break;
   }
-  // Frechet pairs use 4 x 4 tiles (more threads per matrix for the same shared state).
+  // Tile shapes (TM x TN per thread) and warps per team, chosen by measurement on B200:
+  // more warps per SM beat larger per-thread tiles as long as the shared-memory wavefront
+  // budget holds.  32 x 32: forward 4 x 4 tiles in two-warp teams, Frechet 2 x 4 tiles in
+  // four-warp teams (20 warps per SM at 40 KB of shared state per matrix).
   constexpr int TN = Pair ? 4 : 8;
-  if (n <= 8) return launch_team<8, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
-  if (n <= 16) return launch_team<16, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
-  return launch_team<32, TN, Pair, Pair ? 2 : 1>(a, e, out, batch, n, dtype, stream);
+  if (n <= 8) return launch_team<8, 4, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  if (n <= 16) return launch_team<16, 4, TN, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  if constexpr (Pair) {
+    return launch_team<32, 2, 4, true, 4>(a, e, out, batch, n, dtype, stream);
+  } else {
+    return launch_team<32, 4, 4, false, 2>(a, e, out, batch, n, dtype, stream);
+  }
 }
 
 int check_common(int64_t batch, int32_t n, int32_t dtype, const void* out) {

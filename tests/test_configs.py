@@ -60,11 +60,20 @@ def test_config_full_size_properties(index):
     cfg = W.CONFIGS[index]
     a, g = W.generate(cfg, 0, cfg.batch, device="cuda")
     y, grad = _fwd_bwd(a, g)
-    assert y.isfinite().all() and grad.isfinite().all()
+    # Non-finite outputs are allowed only where the float64 result itself exceeds the output
+    # dtype's range (config 5's lognormal scaling reaches ||A|| ~ 100 for a few matrices in a
+    # million, and exp(A) then overflows float32).
+    limit = torch.finfo(cfg.dtype).max
+    for out, ref_fn in ((y, lambda i: O.exp_fp64(a[i])), (grad, lambda i: O.frechet_fp64(a[i].mT, g[i]))):
+        bad = (~out.flatten(-2).isfinite().all(-1)).nonzero().flatten()
+        assert bad.numel() <= 64, bad.numel()
+        if bad.numel():
+            ref = ref_fn(bad.cpu())
+            assert (ref.flatten(-2).abs().amax(-1) > limit).all(), "non-finite output for a representable result"
     k = PREFIX[index]
     y_pre, grad_pre = _fwd_bwd(a[:k], g[:k])
-    torch.testing.assert_close(y[:k], y_pre, atol=0, rtol=0)
-    torch.testing.assert_close(grad[:k], grad_pre, atol=0, rtol=0)
+    torch.testing.assert_close(y[:k], y_pre, atol=0, rtol=0, equal_nan=True)
+    torch.testing.assert_close(grad[:k], grad_pre, atol=0, rtol=0, equal_nan=True)
     if index == 4:
         ortho = torch.zeros((), device="cuda", dtype=torch.float64)
         for lo in range(0, cfg.batch, 65536):
