@@ -52,11 +52,16 @@ def parse_args():
 # distributed plumbing
 # ----------------------------------------------------------------------------------------
 class Dist:
+    """One process per GPU (torchrun env vars); NCCL for GPU runs, gloo for the CPU arm.
+    Collectives are used only outside the timed region: barriers around it and a MAX
+    all-reduce of the per-rank times."""
+
     def __init__(self):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
+        self.backend = None
 
     def init(self, backend: str):
         if self.world > 1:
@@ -66,10 +71,11 @@ class Dist:
 
             dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=300))
             self.pg = dist
+            self.backend = backend
 
     def barrier(self):
         if self.pg is not None:
-            if torch.cuda.is_available():
+            if self.backend == "nccl":
                 self.pg.barrier(device_ids=[self.local_rank])
             else:
                 self.pg.barrier()
@@ -77,7 +83,8 @@ class Dist:
     def max(self, value: float) -> float:
         if self.pg is None:
             return value
-        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        device = f"cuda:{self.local_rank}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([value], dtype=torch.float64, device=device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -329,6 +336,7 @@ def cpu_reference_sample(cfg, target_seconds: float):
     torch.set_num_threads(threads)
     probe = 256 if cfg.n >= 16 else 2048
     a, g = W.generate(cfg, 0, min(probe, cfg.batch), device="cpu")
+    cpu_path.time_fwd_bwd(a, g, repeat=1)  # first call pays one-time thread-pool costs
     t = cpu_path.time_fwd_bwd(a, g, repeat=1)
     rate = a.shape[0] / t
     count = int(min(cfg.batch, max(probe, rate * target_seconds)))
@@ -353,6 +361,7 @@ def run_reference(args, dist):
     per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
     probe = 256 if cfg.n >= 16 else 2048
     a, g = W.generate(cfg, 0, min(probe, cfg.batch), device="cpu")
+    cpu_path.time_fwd_bwd(a, g, repeat=1)  # first call pays one-time thread-pool costs
     rate = a.shape[0] / cpu_path.time_fwd_bwd(a, g, repeat=1)
     count = int(min(cfg.batch, max(probe, rate * per_step)))
     count = max(probe, (count // probe) * probe) if count >= probe else count
