@@ -135,15 +135,20 @@ struct TeamCfg {
   static constexpr int QR = (T < 8) ? 1 : (TN >= TM ? (RB >= 4 ? 4 : RB) : 2);
   static constexpr int QC = (T < 8) ? 1 : 8 / QR;
   static_assert(T < 8 || (RB % QR == 0 && CB % QC == 0 && QR * QC == 8), "quarter-warp tiling");
+  // Row blocks of one quarter-warp are RB / QR apart (e.g. 0, 4, 8, 12 of 16), so that with
+  // TM = 2 they still fall in different 4-row rotation groups.
+  static_assert(T < 8 || TM * (RB / QR) >= 4 || QR == 1, "quarter rows must span rotation groups");
   static_assert(TEAM_FLOATS % 4 == 0, "16-byte aligned team regions");
 };
 
 // Offset of element (i, j) inside a plane: 16-byte chunk (j / 4) of row i is stored at
-// chunk position (j / 4) ^ (i / TM), TM the height of a thread's tile.  The TM rows of one
-// tile share a rotation; the row blocks of a warp get different ones.
+// chunk position (j / 4) ^ (i / 4).  Rows of one 4-row group share a rotation, so a thread
+// reads a row chunk of Y for four consecutive k with one address computation; the thread ->
+// tile map spreads the row blocks of a quarter-warp over different 4-row groups, so their X
+// reads hit different bank groups.  (TM is kept as a parameter of the call sites.)
 template <int P, int TM>
 __device__ __forceinline__ int pidx(int i, int j) {
-  return i * P + ((((j >> 2) ^ (i / TM)) & (P / 4 - 1)) << 2) + (j & 3);
+  return i * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
 }
 
 template <int T>
@@ -221,15 +226,18 @@ __device__ __forceinline__ unsigned smem_addr(const float* p) {
 }
 
 // R += X Y.  X, Y: first (value) plane of a slot; the derivative plane follows at +PLANE.
+// Per group of four k: the TM x 4 block of X (TM 128-bit loads) and, for each of the
+// thread's TN/4 column chunks, rows 4q..4q+3 of Y at one rotated chunk position.
 template <int P, int TM, int TN, bool Pair>
 __device__ __forceinline__ void team_product(const float* __restrict__ X, const float* __restrict__ Y, int i0, int j0,
                                              Acc<TM, TN, Pair>& R) {
   constexpr unsigned PLANE_B = P * P * 4;  // bytes
-  constexpr int MASK = P / 4 - 1;
-  const int rb = i0 / TM;
-  const int c0 = j0 >> 2;
-  const unsigned xrow = smem_addr(X) + unsigned(i0 * P) * 4u;
-  const unsigned ybase = smem_addr(Y);
+  constexpr unsigned ROW_B = P * 4;
+  constexpr unsigned MASK16 = unsigned(P / 4 - 1) << 4;
+  const unsigned rx16 = unsigned(i0 >> 2) << 4;  // rotation of the thread's X rows (bytes)
+  const unsigned c016 = unsigned(j0 >> 2) << 4;  // first column chunk of the tile (bytes)
+  const unsigned xrow = smem_addr(X) + unsigned(i0) * ROW_B;
+  unsigned yrow = smem_addr(Y);
   // Frechet: R.u accumulates X dY, V accumulates dX Y (independent FMA chains).
   float V[Pair ? TM : 1][Pair ? TN : 1];
   if constexpr (Pair) {
@@ -239,27 +247,26 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
       for (int jj = 0; jj < TN; ++jj) V[ii][jj] = 0.f;
   }
 #pragma unroll(Pair ? 1 : 2)
-  for (int q = 0; q < P / 4; ++q) {
-    const unsigned xc = unsigned((q ^ rb) & MASK) << 4;
+  for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
+    const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
     float4 xb[TM], xub[TM];
 #pragma unroll
     for (int ii = 0; ii < TM; ++ii) {
-      xb[ii] = lds128(xrow + unsigned(ii * P) * 4u + xc);
-      if constexpr (Pair) xub[ii] = lds128(xrow + PLANE_B + unsigned(ii * P) * 4u + xc);
+      xb[ii] = lds128(xa + unsigned(ii) * ROW_B);
+      if constexpr (Pair) xub[ii] = lds128(xa + PLANE_B + unsigned(ii) * ROW_B);
     }
-    const unsigned yrow = ybase + unsigned(4 * q * P) * 4u;
+    unsigned ya[TN / 4];
+#pragma unroll
+    for (int c = 0; c < TN / 4; ++c) ya[c] = yrow + (((c016 + unsigned(c) * 16u) ^ q16) & MASK16);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      // row k = 4q + r of Y is rotated by k / TM
-      const int rot = (4 * q + r) / TM;
       float y[TN], yu[TN];
 #pragma unroll
       for (int c = 0; c < TN / 4; ++c) {
-        const unsigned yc = unsigned(((c0 + c) ^ rot) & MASK) << 4;
-        const float4 v = lds128(yrow + unsigned(r * P) * 4u + yc);
+        const float4 v = lds128(ya[c] + unsigned(r) * ROW_B);
         y[4 * c] = v.x; y[4 * c + 1] = v.y; y[4 * c + 2] = v.z; y[4 * c + 3] = v.w;
         if constexpr (Pair) {
-          const float4 w = lds128(yrow + PLANE_B + unsigned(r * P) * 4u + yc);
+          const float4 w = lds128(ya[c] + PLANE_B + unsigned(r) * ROW_B);
           yu[4 * c] = w.x; yu[4 * c + 1] = w.y; yu[4 * c + 2] = w.z; yu[4 * c + 3] = w.w;
         }
       }
@@ -278,6 +285,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
         }
       }
     }
+    yrow += 4u * ROW_B;
   }
   if constexpr (Pair) {
 #pragma unroll
@@ -422,7 +430,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     cb = t % C::CB;
   } else {
     const int u = t / 8, v = t % 8;  // quarter-warp u, thread v within it
-    rb = (u / (C::CB / C::QC)) * C::QR + v / C::QC;
+    rb = (v / C::QC) * (C::RB / C::QR) + u / (C::CB / C::QC);
     cb = (u % (C::CB / C::QC)) * C::QC + v % C::QC;
   }
   const int i0 = TM * rb, j0 = TN * cb;
