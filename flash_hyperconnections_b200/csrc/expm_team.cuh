@@ -160,10 +160,11 @@ __device__ __forceinline__ void team_sync(int team_in_cta) {
   }
 }
 
+// Accumulators in float2 pairs along j: one paired FMA (FFMA2, sm_100) updates two of them.
 template <int TM, int TN, bool Pair>
 struct Acc {
-  float d[TM][TN];
-  float u[Pair ? TM : 1][Pair ? TN : 1];
+  float2 d[TM][TN / 2];
+  float2 u[Pair ? TM : 1][Pair ? TN / 2 : 1];
 };
 
 template <int TM, int TN, bool Pair>
@@ -171,13 +172,13 @@ __device__ __forceinline__ void acc_zero(Acc<TM, TN, Pair>& R) {
 #pragma unroll
   for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
-    for (int jj = 0; jj < TN; ++jj) {
-      R.d[ii][jj] = 0.f;
-      if constexpr (Pair) R.u[ii][jj] = 0.f;
+    for (int jj = 0; jj < TN / 2; ++jj) {
+      R.d[ii][jj] = make_float2(0.f, 0.f);
+      if constexpr (Pair) R.u[ii][jj] = make_float2(0.f, 0.f);
     }
 }
 
-// Thread-own tile <-> slot.  Own chunks: rows i0..i0+3, chunks j0/4 .. j0/4 + TN/4 - 1.
+// Thread-own tile <-> slot.  Own chunks: rows i0..i0+TM-1, chunks j0/4 .. j0/4 + TN/4 - 1.
 template <int P, int TM, int TN, bool Pair>
 __device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int j0, const Acc<TM, TN, Pair>& R) {
 #pragma unroll
@@ -186,10 +187,10 @@ __device__ __forceinline__ void acc_store(float* __restrict__ slot, int i0, int 
     for (int c = 0; c < TN / 4; ++c) {
       const int o = pidx<P, TM>(i0 + ii, j0 + 4 * c);
       *reinterpret_cast<float4*>(slot + o) =
-          make_float4(R.d[ii][4 * c], R.d[ii][4 * c + 1], R.d[ii][4 * c + 2], R.d[ii][4 * c + 3]);
+          make_float4(R.d[ii][2 * c].x, R.d[ii][2 * c].y, R.d[ii][2 * c + 1].x, R.d[ii][2 * c + 1].y);
       if constexpr (Pair)
         *reinterpret_cast<float4*>(slot + P * P + o) =
-            make_float4(R.u[ii][4 * c], R.u[ii][4 * c + 1], R.u[ii][4 * c + 2], R.u[ii][4 * c + 3]);
+            make_float4(R.u[ii][2 * c].x, R.u[ii][2 * c].y, R.u[ii][2 * c + 1].x, R.u[ii][2 * c + 1].y);
     }
 }
 
@@ -201,10 +202,12 @@ __device__ __forceinline__ void acc_load(const float* __restrict__ slot, int i0,
     for (int c = 0; c < TN / 4; ++c) {
       const int o = pidx<P, TM>(i0 + ii, j0 + 4 * c);
       const float4 a = *reinterpret_cast<const float4*>(slot + o);
-      R.d[ii][4 * c] = a.x; R.d[ii][4 * c + 1] = a.y; R.d[ii][4 * c + 2] = a.z; R.d[ii][4 * c + 3] = a.w;
+      R.d[ii][2 * c] = make_float2(a.x, a.y);
+      R.d[ii][2 * c + 1] = make_float2(a.z, a.w);
       if constexpr (Pair) {
         const float4 b = *reinterpret_cast<const float4*>(slot + P * P + o);
-        R.u[ii][4 * c] = b.x; R.u[ii][4 * c + 1] = b.y; R.u[ii][4 * c + 2] = b.z; R.u[ii][4 * c + 3] = b.w;
+        R.u[ii][2 * c] = make_float2(b.x, b.y);
+        R.u[ii][2 * c + 1] = make_float2(b.z, b.w);
       }
     }
 }
@@ -239,12 +242,12 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   const unsigned xrow = smem_addr(X) + unsigned(i0) * ROW_B;
   unsigned yrow = smem_addr(Y);
   // Frechet: R.u accumulates X dY, V accumulates dX Y (independent FMA chains).
-  float V[Pair ? TM : 1][Pair ? TN : 1];
+  float2 V[Pair ? TM : 1][Pair ? TN / 2 : 1];
   if constexpr (Pair) {
 #pragma unroll
     for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
-      for (int jj = 0; jj < TN; ++jj) V[ii][jj] = 0.f;
+      for (int jj = 0; jj < TN / 2; ++jj) V[ii][jj] = make_float2(0.f, 0.f);
   }
 #pragma unroll(Pair ? 1 : 2)
   for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
@@ -260,27 +263,30 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
     for (int c = 0; c < TN / 4; ++c) ya[c] = yrow + (((c016 + unsigned(c) * 16u) ^ q16) & MASK16);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      float y[TN], yu[TN];
+      float2 y[TN / 2], yu[TN / 2];
 #pragma unroll
       for (int c = 0; c < TN / 4; ++c) {
         const float4 v = lds128(ya[c] + unsigned(r) * ROW_B);
-        y[4 * c] = v.x; y[4 * c + 1] = v.y; y[4 * c + 2] = v.z; y[4 * c + 3] = v.w;
+        y[2 * c] = make_float2(v.x, v.y);
+        y[2 * c + 1] = make_float2(v.z, v.w);
         if constexpr (Pair) {
           const float4 w = lds128(ya[c] + PLANE_B + unsigned(r) * ROW_B);
-          yu[4 * c] = w.x; yu[4 * c + 1] = w.y; yu[4 * c + 2] = w.z; yu[4 * c + 3] = w.w;
+          yu[2 * c] = make_float2(w.x, w.y);
+          yu[2 * c + 1] = make_float2(w.z, w.w);
         }
       }
 #pragma unroll
       for (int ii = 0; ii < TM; ++ii) {
         const float x = f4get(xb[ii], r);
-        float xu = 0.f;
-        if constexpr (Pair) xu = f4get(xub[ii], r);
+        const float2 x2 = make_float2(x, x);
+        float2 xu2 = make_float2(0.f, 0.f);
+        if constexpr (Pair) xu2 = make_float2(f4get(xub[ii], r), f4get(xub[ii], r));
 #pragma unroll
-        for (int jj = 0; jj < TN; ++jj) {
-          R.d[ii][jj] = fmaf(x, y[jj], R.d[ii][jj]);
+        for (int jj = 0; jj < TN / 2; ++jj) {
+          R.d[ii][jj] = __ffma2_rn(x2, y[jj], R.d[ii][jj]);
           if constexpr (Pair) {
-            R.u[ii][jj] = fmaf(x, yu[jj], R.u[ii][jj]);
-            V[ii][jj] = fmaf(xu, y[jj], V[ii][jj]);
+            R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
+            V[ii][jj] = __ffma2_rn(xu2, y[jj], V[ii][jj]);
           }
         }
       }
@@ -291,7 +297,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
 #pragma unroll
     for (int ii = 0; ii < TM; ++ii)
 #pragma unroll
-      for (int jj = 0; jj < TN; ++jj) R.u[ii][jj] += V[ii][jj];
+      for (int jj = 0; jj < TN / 2; ++jj) R.u[ii][jj] = __fadd2_rn(R.u[ii][jj], V[ii][jj]);
   }
 }
 
@@ -495,66 +501,69 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     fetch(item + gridDim.x);  // next matrix of this team: loads stay in flight during the steps
     if (bad) scratch[3] = 1;
     team_sync<T>(tic);
-    // ---- norms: thread t < P sums |row t| and |column t| of A in float64 ----
+    // ---- norms: sums of |row| and |column| of A, maxima over the team ----
     // Sums of |a| in four float32 partial sums combined in float64; a partial sum that
-    // overflows float32 (entries near the float32 limit) is redone in float64.
+    // overflows float32 (entries near the float32 limit) is redone in float64.  Teams of at
+    // least 2P threads split the work: threads 0..P-1 rows, P..2P-1 columns.
+    auto line_sum = [&](int l, bool column) {
+      // element k of line l: a[l][k] for a row, a[k][l] for a column
+      auto at = [&](int k) { return team[column ? pidx<P, TM>(k, l) : pidx<P, TM>(l, k)]; };
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < P; ++k) ps[k & 3] += fabsf(at(k));
+      double sum = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
+      if (!isfinite(sum)) {
+        sum = 0.0;
+#pragma unroll 1
+        for (int k = 0; k < P; ++k) sum += fabs(double(at(k)));
+      }
+      return sum;
+    };
+    static_assert(T <= 32 || (P == 32 && T >= 2 * P), "team norm split");
     double nrow = 0.0, ncol = 0.0;
-    for (int l = t; l < P; l += T) {
-      float rs[4] = {0.f, 0.f, 0.f, 0.f}, cs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c4 = 0; c4 < P / 4; ++c4) {
-        const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(l, 4 * c4));
-        rs[0] += fabsf(x.x);
-        rs[1] += fabsf(x.y);
-        rs[2] += fabsf(x.z);
-        rs[3] += fabsf(x.w);
+    if constexpr (T >= 2 * P) {
+      if (t < P) {
+        nrow = line_sum(t, false);
+      } else if (t < 2 * P) {
+        ncol = line_sum(t - P, true);
       }
-#pragma unroll
-      for (int r = 0; r < P; ++r) cs[r & 3] += fabsf(team[pidx<P, TM>(r, l)]);
-      double rsum = (double(rs[0]) + double(rs[1])) + (double(rs[2]) + double(rs[3]));
-      double csum = (double(cs[0]) + double(cs[1])) + (double(cs[2]) + double(cs[3]));
-      if (!isfinite(rsum) || !isfinite(csum)) {
-        rsum = csum = 0.0;
-        for (int r = 0; r < P; ++r) {
-          rsum += fabs(double(team[pidx<P, TM>(l, r)]));
-          csum += fabs(double(team[pidx<P, TM>(r, l)]));
-        }
+    } else {
+      for (int l = t; l < P; l += T) {
+        nrow = fmax(nrow, line_sum(l, false));
+        ncol = fmax(ncol, line_sum(l, true));
       }
-      nrow = fmax(nrow, rsum);
-      ncol = fmax(ncol, csum);
     }
     int m = 1, s = 0, nsteps = 0;
-    constexpr int RED = T < P ? T : P;  // threads 0 .. RED-1 hold norms, all in one warp
-    if (t < 32) {
+    if constexpr (T <= 32) {
+      constexpr int RED = T < P ? T : P;  // threads 0 .. RED-1 of the team hold norms
 #pragma unroll
       for (int off = 1; off < RED; off <<= 1) {
         nrow = fmax(nrow, __shfl_xor_sync(0xffffffffu, nrow, off));
         ncol = fmax(ncol, __shfl_xor_sync(0xffffffffu, ncol, off));
       }
-    }
-    if constexpr (T <= 32) {
-      choose_degree(fmin(nrow, ncol), &m, &s);
-      const bool team_bad = scratch[3] != 0;
-      nsteps = (valid && !team_bad) ? scheme_products(m) + s : (team_bad ? -1 : 0);
     } else {
-      if (t == 0) {
-        choose_degree(fmin(nrow, ncol), &m, &s);
-        const bool team_bad = scratch[3] != 0;
-        scratch[0] = m;
-        scratch[1] = s;
-        scratch[2] = (valid && !team_bad) ? scheme_products(m) + s : (team_bad ? -1 : 0);
+      // warp 0 holds the row sums, warp 1 the column sums (P = 32)
+      double* maxima = reinterpret_cast<double*>(scratch + 4);
+      if (t < 64) {
+        double v = t < 32 ? nrow : ncol;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if ((t & 31) == 0) maxima[t >> 5] = v;
       }
-      team_sync<T>(tic);
-      m = scratch[0];
-      s = scratch[1];
-      nsteps = scratch[2];
+      team_sync<T>(tic);  // also: every column read is done before tiles are rescaled
+      nrow = maxima[0];
+      ncol = maxima[1];
+    }
+    choose_degree(fmin(nrow, ncol), &m, &s);
+    {
+      const bool bad_team = scratch[3] != 0;
+      nsteps = (valid && !bad_team) ? scheme_products(m) + s : (bad_team ? -1 : 0);
     }
     const bool team_bad = nsteps < 0;
     if (team_bad) nsteps = 0;
     const int poly = scheme_products(m);
     const int prog = program_offset(m);
-    team_sync<T>(tic);  // every column read is done before tiles are rescaled
-    if (t == 0) scratch[3] = 0;  // non-finite flag, free for the next matrix
+    if constexpr (T <= 32) team_sync<T>(tic);  // every column read is done before tiles are rescaled
 
     // ---- A / 2^s (own tile), identity for the degree-1 polynomial ----
     if (s > 0 || m == 1) {
@@ -582,18 +591,24 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
       }
     }
     team_sync<T>(tic);
+    if (t == 0) scratch[3] = 0;  // non-finite flag: every thread has read it; free for the next matrix
 
     // ---- polynomial steps, then squarings ----
+    // Whole-warp teams square in ping-pong between slots 0 and 1: the slot written in a
+    // squaring step is not read in it, so one barrier per squaring suffices.  Teams that
+    // share a warp keep the lockstep two-barrier form.
+    constexpr bool kPingPong = T >= 32;
     int max_steps = nsteps;
     if constexpr (T < 32) max_steps = __reduce_max_sync(0xffffffffu, nsteps);
+    int cur = 0;  // slot holding the current value during the squarings
     for (int st = 0; st < max_steps; ++st) {
       const bool active = st < nsteps;
       const bool is_poly = st < poly;
       const Step* step = &kSteps[prog + (is_poly ? st : 0)];
-      const int xs = is_poly ? step->x : 0;
-      const int ys = is_poly ? step->y : 0;
+      const int xs = is_poly ? step->x : cur;
+      const int ys = is_poly ? step->y : cur;
       const int zs = is_poly ? step->z : -1;
-      const int rs = is_poly ? step->r : 0;
+      const int rs = is_poly ? step->r : (kPingPong ? 1 - cur : 0);
       Acc<TM, TN, Pair> R;
       if (active) {
         if (zs >= 0) {
@@ -603,17 +618,18 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
         }
         team_product<P, TM, TN, Pair>(team + xs * C::SLOT, team + ys * C::SLOT, i0, j0, R);
       }
-      team_sync<T>(tic);
+      if (!kPingPong || is_poly) team_sync<T>(tic);
       if (active) {
         acc_store<P, TM, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
         if (is_poly && step->nout > 0) team_epilogue<P, TM, TN, Pair>(prog + st, team, i0, j0);
       }
       team_sync<T>(tic);
+      if (!is_poly) cur = rs;
     }
 
     // ---- the n x n result, 16-byte chunks spread over the team ----
     if (valid) {
-      const float* res = team + (Pair ? C::PLANE : 0);
+      const float* res = team + cur * C::SLOT + (Pair ? C::PLANE : 0);
       const float nanv = __int_as_float(0x7fc00000);
 #pragma unroll 1
       for (int idx = t; idx < n * (P / 4); idx += T) {
@@ -633,9 +649,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
         }
       }
     }
-    team_sync<T>(tic);
-    if (t == 0) scratch[3] = 0;
-    team_sync<T>(tic);
+    team_sync<T>(tic);  // the result slot is read before the next matrix is written
   }
 }
 

@@ -81,12 +81,20 @@ def _setup_context(ctx, inputs, output):
     ctx.save_for_backward(inputs[0])
 
 
+def _has_tangent(t) -> bool:
+    # Outside every forward-AD level no tensor can carry a tangent; unpack_dual would
+    # return None, so the (comparatively slow) call is skipped.
+    if torch.autograd.forward_ad._current_level < 0:
+        return False
+    return torch.autograd.forward_ad.unpack_dual(t).tangent is not None
+
+
 def _needs_differentiable_backward(input, grad_output) -> bool:
     return (
         torch.is_grad_enabled()
         or has_torch_function((input, grad_output))
-        or torch.autograd.forward_ad.unpack_dual(input).tangent is not None
-        or torch.autograd.forward_ad.unpack_dual(grad_output).tangent is not None
+        or _has_tangent(input)
+        or _has_tangent(grad_output)
     )
 
 
@@ -115,7 +123,7 @@ def matrix_exp(input: torch.Tensor) -> torch.Tensor:
     if isinstance(input, torch.Tensor) and (
         type(input) not in (torch.Tensor, torch.nn.Parameter)
         or torch._C._are_functorch_transforms_active()
-        or torch.autograd.forward_ad.unpack_dual(input).tangent is not None
+        or _has_tangent(input)
     ):
         return _native(input, promote=True)
     if not _eligible(input):
