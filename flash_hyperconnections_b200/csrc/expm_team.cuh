@@ -68,48 +68,58 @@ struct Step {
 
 // Programs for m = 2, 4, 8, 12, 18 (steps numbered from 0; the result ends in slot 0).
 // Slots: 0 holds A on entry.  Coefficients: BBC 2019 schemes, expm_coeffs.h.
-__constant__ Step kSteps[15] = {
-    // m = 2: A2 -> s1; s0 = I + A + A2/2
-    {0, 0, -1, 1, 2, 1, {0, 1}, {0}, {{1.f, 1.f, 0.5f}}},
-    // m = 4: A2 -> s1; s2 = I/2 + A/6 + A2/24, s3 = I + A
-    {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.5f, 1.f / 6.f, 1.f / 24.f}, {1.f, 1.f, 0.f}}},
-    //         s0 = A2 * s2 + s3
-    {1, 2, 3, 0, 0, 0, {}, {}, {}},
-    // m = 8: A2 -> s1; s2 = x1 A + x2 A2 (C1), s3 = I + A + y2 A2 (F)
-    {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.f, kT8X1, kT8X2}, {1.f, 1.f, kT8Y2}}},
-    //         A4 = A2 * C1 -> s4; s2 = x3 A2 + A4 (L), s0 = x4 I + x5 A + x6 A2 + x7 A4 (R)
-    {1, 2, -1, 4, 3, 2, {0, 1, 4}, {2, 0}, {{0.f, 0.f, kT8X3, 1.f}, {kT8X4, kT8X5, kT8X6, kT8X7}}},
-    //         s0 = L * R + F
-    {2, 0, 3, 0, 0, 0, {}, {}, {}},
-    // m = 12: A2 -> s1
-    {0, 0, -1, 1, 0, 0, {}, {}, {}},
-    //          A3 -> s2; s3 = B4, s4 = B3, s1 = B2, s0 = B1 (on I, A, A2, A3)
-    {1, 0, -1, 2, 3, 4, {0, 1, 2}, {3, 4, 1, 0},
-     {{t12c(3, 0), t12c(3, 1), t12c(3, 2), t12c(3, 3)},
-      {t12c(2, 0), t12c(2, 1), t12c(2, 2), t12c(2, 3)},
-      {t12c(1, 0), t12c(1, 1), t12c(1, 2), t12c(1, 3)},
-      {t12c(0, 0), t12c(0, 1), t12c(0, 2), t12c(0, 3)}}},
-    //          A6 = B4 * B4 + B3 -> s2; s1 = B2 + A6
-    {3, 3, 4, 2, 2, 1, {1, 2}, {1}, {{0.f, 1.f, 1.f}}},
-    //          s0 = (B2 + A6) * A6 + B1
-    {1, 2, 0, 0, 0, 0, {}, {}, {}},
-    // m = 18: A2 -> s1
-    {0, 0, -1, 1, 0, 0, {}, {}, {}},
-    //          A3 -> s2
-    {1, 0, -1, 2, 0, 0, {}, {}, {}},
-    //          A6 -> s3; s0 = B1, s1 = B5, s2 = B4, s3 = B3 + B4, s4 = B2 (on I, A, A2, A3, A6)
-    {2, 2, -1, 3, 4, 5, {0, 1, 2, 3}, {0, 1, 2, 3, 4},
-     {{t18c(0, 0), t18c(0, 1), t18c(0, 2), t18c(0, 3), t18c(0, 4)},
-      {t18c(4, 0), t18c(4, 1), t18c(4, 2), t18c(4, 3), t18c(4, 4)},
-      {t18c(3, 0), t18c(3, 1), t18c(3, 2), t18c(3, 3), t18c(3, 4)},
-      {t18c(2, 0) + t18c(3, 0), t18c(2, 1) + t18c(3, 1), t18c(2, 2) + t18c(3, 2), t18c(2, 3) + t18c(3, 3),
-       t18c(2, 4) + t18c(3, 4)},
-      {t18c(1, 0), t18c(1, 1), t18c(1, 2), t18c(1, 3), t18c(1, 4)}}},
-    //          P = B1 * B5 -> s0; s1 = P + B4 (A9), s0 = P + B3 + B4
-    {0, 1, -1, 0, 3, 2, {0, 2, 3}, {1, 0}, {{0.f, 1.f, 1.f, 0.f}, {0.f, 1.f, 0.f, 1.f}}},
-    //          s0 = (B3 + A9) * A9 + B2
-    {0, 1, 4, 0, 0, 0, {}, {}, {}},
-};
+constexpr int kNumSteps = 15;
+__host__ __device__ constexpr Step step_def(int index) {
+  constexpr Step tab[kNumSteps] = {
+      // m = 2: A2 -> s1; s0 = I + A + A2/2
+      {0, 0, -1, 1, 2, 1, {0, 1}, {0}, {{1.f, 1.f, 0.5f}}},
+      // m = 4: A2 -> s1; s2 = I/2 + A/6 + A2/24, s3 = I + A
+      {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.5f, 1.f / 6.f, 1.f / 24.f}, {1.f, 1.f, 0.f}}},
+      //         s0 = A2 * s2 + s3
+      {1, 2, 3, 0, 0, 0, {}, {}, {}},
+      // m = 8: A2 -> s1; s2 = x1 A + x2 A2 (C1), s3 = I + A + y2 A2 (F)
+      {0, 0, -1, 1, 2, 2, {0, 1}, {2, 3}, {{0.f, kT8X1, kT8X2}, {1.f, 1.f, kT8Y2}}},
+      //         A4 = A2 * C1 -> s4; s2 = x3 A2 + A4 (L), s0 = x4 I + x5 A + x6 A2 + x7 A4 (R)
+      {1, 2, -1, 4, 3, 2, {0, 1, 4}, {2, 0}, {{0.f, 0.f, kT8X3, 1.f}, {kT8X4, kT8X5, kT8X6, kT8X7}}},
+      //         s0 = L * R + F
+      {2, 0, 3, 0, 0, 0, {}, {}, {}},
+      // m = 12: A2 -> s1
+      {0, 0, -1, 1, 0, 0, {}, {}, {}},
+      //          A3 -> s2; s3 = B4, s4 = B3, s1 = B2, s0 = B1 (on I, A, A2, A3)
+      {1, 0, -1, 2, 3, 4, {0, 1, 2}, {3, 4, 1, 0},
+       {{t12c(3, 0), t12c(3, 1), t12c(3, 2), t12c(3, 3)},
+        {t12c(2, 0), t12c(2, 1), t12c(2, 2), t12c(2, 3)},
+        {t12c(1, 0), t12c(1, 1), t12c(1, 2), t12c(1, 3)},
+        {t12c(0, 0), t12c(0, 1), t12c(0, 2), t12c(0, 3)}}},
+      //          A6 = B4 * B4 + B3 -> s2; s1 = B2 + A6
+      {3, 3, 4, 2, 2, 1, {1, 2}, {1}, {{0.f, 1.f, 1.f}}},
+      //          s0 = (B2 + A6) * A6 + B1
+      {1, 2, 0, 0, 0, 0, {}, {}, {}},
+      // m = 18: A2 -> s1
+      {0, 0, -1, 1, 0, 0, {}, {}, {}},
+      //          A3 -> s2
+      {1, 0, -1, 2, 0, 0, {}, {}, {}},
+      //          A6 -> s3; s0 = B1, s1 = B5, s2 = B4, s3 = B3 + B4, s4 = B2 (on I, A, A2, A3, A6)
+      {2, 2, -1, 3, 4, 5, {0, 1, 2, 3}, {0, 1, 2, 3, 4},
+       {{t18c(0, 0), t18c(0, 1), t18c(0, 2), t18c(0, 3), t18c(0, 4)},
+        {t18c(4, 0), t18c(4, 1), t18c(4, 2), t18c(4, 3), t18c(4, 4)},
+        {t18c(3, 0), t18c(3, 1), t18c(3, 2), t18c(3, 3), t18c(3, 4)},
+        {t18c(2, 0) + t18c(3, 0), t18c(2, 1) + t18c(3, 1), t18c(2, 2) + t18c(3, 2), t18c(2, 3) + t18c(3, 3),
+         t18c(2, 4) + t18c(3, 4)},
+        {t18c(1, 0), t18c(1, 1), t18c(1, 2), t18c(1, 3), t18c(1, 4)}}},
+      //          P = B1 * B5 -> s0; s1 = P + B4 (A9), s0 = P + B3 + B4
+      {0, 1, -1, 0, 3, 2, {0, 2, 3}, {1, 0}, {{0.f, 1.f, 1.f, 0.f}, {0.f, 1.f, 0.f, 1.f}}},
+      //          s0 = (B3 + A9) * A9 + B2
+      {0, 1, 4, 0, 0, 0, {}, {}, {}},
+  };
+  return tab[index];
+}
+
+// Device copy for the step machine (operand slots, output count); the epilogues take their
+// coefficients from step_def at compile time.
+__constant__ Step kSteps[kNumSteps] = {step_def(0),  step_def(1),  step_def(2),  step_def(3),  step_def(4),
+                                       step_def(5),  step_def(6),  step_def(7),  step_def(8),  step_def(9),
+                                       step_def(10), step_def(11), step_def(12), step_def(13), step_def(14)};
 
 __host__ __device__ __forceinline__ int program_offset(int m) {
   return m == 2 ? 0 : m == 4 ? 1 : m == 8 ? 3 : m == 12 ? 6 : 10;
@@ -301,56 +311,78 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   }
 }
 
-// Element-wise linear combinations of a step on the thread's own 4 x TN tile (TN 16-byte
-// chunks per plane).  Kept as a rolled loop: this is the cold part of a step.
-template <int P, int TM, int TN, bool Pair>
-__device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+// Element-wise linear combinations of step S on the thread's own TM x TN tile, with the
+// coefficients of step_def(S) as compile-time constants: zero terms vanish, and each term is
+// one FFMA with an immediate coefficient.  Terms are accumulated in the table's order,
+// identity first.
+template <int P, int TM, int TN, bool Pair, int S>
+__device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, int j0) {
+  constexpr Step st = step_def(S);
   constexpr int PLANE = P * P;
   constexpr int SLOT = TeamCfg<P, TM, TN, Pair>::SLOT;
-  const Step& st = kSteps[step_index];
-  const int nin = st.nin, nout = st.nout;
-  float coef[kMaxOut][kMaxIn + 1];
-  int in_off[kMaxIn], out_off[kMaxOut];
+  constexpr int CH = TM * TN / 4;  // own 16-byte chunks per plane
 #pragma unroll
-  for (int o = 0; o < kMaxOut; ++o) {
-    out_off[o] = st.out[o] * SLOT;
-#pragma unroll
-    for (int t = 0; t < kMaxIn + 1; ++t) coef[o][t] = st.coef[o][t];
-  }
-#pragma unroll
-  for (int t = 0; t < kMaxIn; ++t) in_off[t] = st.in[t] * SLOT;
-#pragma unroll 1
   for (int part = 0; part < (Pair ? 2 : 1); ++part) {
-#pragma unroll 2
-    for (int c = 0; c < TM * TN / 4; ++c) {
+    float4 in[st.nin > 0 ? st.nin : 1][CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int off = part * PLANE + pidx<P, TM>(i0 + c / (TN / 4), j0 + 4 * (c % (TN / 4)));
+#pragma unroll
+      for (int t = 0; t < st.nin; ++t) in[t][c] = *reinterpret_cast<const float4*>(team + st.in[t] * SLOT + off);
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
       const int i = i0 + c / (TN / 4);
       const int j = j0 + 4 * (c % (TN / 4));
       const int off = part * PLANE + pidx<P, TM>(i, j);
       const int dj = part == 0 ? i - j : -1;  // identity pattern of this chunk (value plane only)
       const float4 id = make_float4(dj == 0 ? 1.f : 0.f, dj == 1 ? 1.f : 0.f, dj == 2 ? 1.f : 0.f, dj == 3 ? 1.f : 0.f);
-      float4 in[kMaxIn];
 #pragma unroll
-      for (int t = 0; t < kMaxIn; ++t)
-        if (t < nin) in[t] = *reinterpret_cast<const float4*>(team + in_off[t] + off);
-#pragma unroll
-      for (int o = 0; o < kMaxOut; ++o) {
-        if (o < nout) {
-          const float c0 = coef[o][0];
-          float4 v = make_float4(c0 * id.x, c0 * id.y, c0 * id.z, c0 * id.w);
-#pragma unroll
-          for (int t = 0; t < kMaxIn; ++t) {
-            if (t < nin) {
-              const float cf = coef[o][1 + t];
-              v.x = fmaf(cf, in[t].x, v.x);
-              v.y = fmaf(cf, in[t].y, v.y);
-              v.z = fmaf(cf, in[t].z, v.z);
-              v.w = fmaf(cf, in[t].w, v.w);
-            }
-          }
-          *reinterpret_cast<float4*>(team + out_off[o] + off) = v;
+      for (int o = 0; o < st.nout; ++o) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool first = true;
+        if (st.coef[o][0] != 0.f) {
+          const float c0 = st.coef[o][0];
+          v = make_float4(c0 * id.x, c0 * id.y, c0 * id.z, c0 * id.w);
+          first = false;
         }
+#pragma unroll
+        for (int t = 0; t < st.nin; ++t) {
+          const float cf = st.coef[o][1 + t];
+          if (cf == 0.f) continue;
+          const float4 x = in[t][c];
+          if (first) {
+            v = cf == 1.f ? x : make_float4(cf * x.x, cf * x.y, cf * x.z, cf * x.w);
+            first = false;
+          } else if (cf == 1.f) {
+            v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+          } else {
+            v.x = fmaf(cf, x.x, v.x);
+            v.y = fmaf(cf, x.y, v.y);
+            v.z = fmaf(cf, x.z, v.z);
+            v.w = fmaf(cf, x.w, v.w);
+          }
+        }
+        *reinterpret_cast<float4*>(team + st.out[o] * SLOT + off) = v;
       }
     }
+  }
+}
+
+// The steps that have outputs, dispatched on the runtime step index.  Kept out of line:
+// only one or two of them run per matrix, and the step loop stays compact.
+template <int P, int TM, int TN, bool Pair>
+__device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+  switch (step_index) {
+#define FHX_EPI(S)                                                                           \
+  case S:                                                                                    \
+    if constexpr (step_def(S).nout > 0) epilogue_step<P, TM, TN, Pair, S>(team, i0, j0); \
+    break;
+    FHX_EPI(0) FHX_EPI(1) FHX_EPI(2) FHX_EPI(3) FHX_EPI(4) FHX_EPI(5) FHX_EPI(6) FHX_EPI(7)
+    FHX_EPI(8) FHX_EPI(9) FHX_EPI(10) FHX_EPI(11) FHX_EPI(12) FHX_EPI(13) FHX_EPI(14)
+#undef FHX_EPI
+    default:
+      break;
   }
 }
 
@@ -631,21 +663,40 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     if (valid) {
       const float* res = team + cur * C::SLOT + (Pair ? C::PLANE : 0);
       const float nanv = __int_as_float(0x7fc00000);
-#pragma unroll 1
-      for (int idx = t; idx < n * (P / 4); idx += T) {
-        const int r = idx / (P / 4);
-        const int c = 4 * (idx % (P / 4));
-        if (c >= n) continue;
-        float4 v = *reinterpret_cast<const float4*>(res + pidx<P, TM>(r, c));
-        if (team_bad) v = make_float4(nanv, nanv, nanv, nanv);
-        const int64_t o = (b * n + r) * int64_t(n) + c;
-        if (out_vec) {
-          store_chunk(out, dtype, o, v);
-        } else {
-          const float vals[4] = {v.x, v.y, v.z, v.w};
+      if (T >= 32 && out_vec && n == P) {
+        // Full-size tile: every chunk exists; all shared loads issue before the stores.
+        constexpr int RES_PER_THREAD = (P * P / 4 + T - 1) / T;
+        float4 v[RES_PER_THREAD];
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (c + u < n) store_elem(out, dtype, o + u, vals[u]);
+        for (int k = 0; k < RES_PER_THREAD; ++k) {
+          const int idx = t + k * T;
+          if (idx < P * P / 4) v[k] = *reinterpret_cast<const float4*>(res + pidx<P, TM>(idx / (P / 4), 4 * (idx % (P / 4))));
+        }
+#pragma unroll
+        for (int k = 0; k < RES_PER_THREAD; ++k) {
+          const int idx = t + k * T;
+          if (idx < P * P / 4) {
+            if (team_bad) v[k] = make_float4(nanv, nanv, nanv, nanv);
+            store_chunk(out, dtype, b * (P * P) + 4 * idx, v[k]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int idx = t; idx < n * (P / 4); idx += T) {
+          const int r = idx / (P / 4);
+          const int c = 4 * (idx % (P / 4));
+          if (c >= n) continue;
+          float4 v = *reinterpret_cast<const float4*>(res + pidx<P, TM>(r, c));
+          if (team_bad) v = make_float4(nanv, nanv, nanv, nanv);
+          const int64_t o = (b * n + r) * int64_t(n) + c;
+          if (out_vec) {
+            store_chunk(out, dtype, o, v);
+          } else {
+            const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (c + u < n) store_elem(out, dtype, o + u, vals[u]);
+          }
         }
       }
     }
