@@ -340,27 +340,59 @@ __device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, 
 #pragma unroll
       for (int o = 0; o < st.nout; ++o) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        bool first = true;
-        if (st.coef[o][0] != 0.f) {
-          const float c0 = st.coef[o][0];
-          v = make_float4(c0 * id.x, c0 * id.y, c0 * id.z, c0 * id.w);
-          first = false;
-        }
-#pragma unroll
-        for (int t = 0; t < st.nin; ++t) {
-          const float cf = st.coef[o][1 + t];
-          if (cf == 0.f) continue;
-          const float4 x = in[t][c];
-          if (first) {
-            v = cf == 1.f ? x : make_float4(cf * x.x, cf * x.y, cf * x.z, cf * x.w);
+        if constexpr (P <= 16) {
+          // (x, y) and (z, w) halves, two lanes per paired FMA: at small P these O(P^2)
+          // combinations are a large share of the work per matrix.
+          float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+          bool first = true;
+          if (st.coef[o][0] != 0.f) {
+            const float c0 = st.coef[o][0];
+            lo = make_float2(c0 * id.x, c0 * id.y);
+            hi = make_float2(c0 * id.z, c0 * id.w);
             first = false;
-          } else if (cf == 1.f) {
-            v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
-          } else {
-            v.x = fmaf(cf, x.x, v.x);
-            v.y = fmaf(cf, x.y, v.y);
-            v.z = fmaf(cf, x.z, v.z);
-            v.w = fmaf(cf, x.w, v.w);
+          }
+#pragma unroll
+          for (int t = 0; t < st.nin; ++t) {
+            const float cf = st.coef[o][1 + t];
+            if (cf == 0.f) continue;
+            const float2 xl = make_float2(in[t][c].x, in[t][c].y), xh = make_float2(in[t][c].z, in[t][c].w);
+            const float2 c2 = make_float2(cf, cf);
+            if (first) {
+              lo = cf == 1.f ? xl : __fmul2_rn(c2, xl);
+              hi = cf == 1.f ? xh : __fmul2_rn(c2, xh);
+              first = false;
+            } else if (cf == 1.f) {
+              lo = __fadd2_rn(lo, xl);
+              hi = __fadd2_rn(hi, xh);
+            } else {
+              lo = __ffma2_rn(c2, xl, lo);
+              hi = __ffma2_rn(c2, xh, hi);
+            }
+          }
+          v = make_float4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+          bool first = true;
+          if (st.coef[o][0] != 0.f) {
+            const float c0 = st.coef[o][0];
+            v = make_float4(c0 * id.x, c0 * id.y, c0 * id.z, c0 * id.w);
+            first = false;
+          }
+#pragma unroll
+          for (int t = 0; t < st.nin; ++t) {
+            const float cf = st.coef[o][1 + t];
+            if (cf == 0.f) continue;
+            const float4 x = in[t][c];
+            if (first) {
+              v = cf == 1.f ? x : make_float4(cf * x.x, cf * x.y, cf * x.z, cf * x.w);
+              first = false;
+            } else if (cf == 1.f) {
+              v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+            } else {
+              v.x = fmaf(cf, x.x, v.x);
+              v.y = fmaf(cf, x.y, v.y);
+              v.z = fmaf(cf, x.z, v.z);
+              v.w = fmaf(cf, x.w, v.w);
+            }
           }
         }
         *reinterpret_cast<float4*>(team + st.out[o] * SLOT + off) = v;
@@ -444,8 +476,9 @@ __device__ __forceinline__ bool finite4(const float4& x) {
 template <int P, int TM, int TN, bool Pair, int WARPS>
 constexpr int team_min_blocks() {
   constexpr int smem = (WARPS * 32 / TeamCfg<P, TM, TN, Pair>::T) * TeamCfg<P, TM, TN, Pair>::TEAM_FLOATS * 4 + 1024;
-  // Only whole-warp teams get the bound; small teams keep their prefetch registers.
-  if constexpr (TeamCfg<P, TM, TN, Pair>::T < 32) return 1;
+  // Frechet teams smaller than a warp keep their registers (measured: the bound costs more in
+  // spills than the extra resident warps return); every other shape gets the bound.
+  if constexpr (Pair && TeamCfg<P, TM, TN, Pair>::T < 32) return 1;
   return (228 * 1024) / smem > 16 ? 16 : (228 * 1024) / smem;
 }
 
@@ -535,8 +568,8 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     team_sync<T>(tic);
     // ---- norms: sums of |row| and |column| of A, maxima over the team ----
     // Sums of |a| in four float32 partial sums combined in float64; a partial sum that
-    // overflows float32 (entries near the float32 limit) is redone in float64.  Teams of at
-    // least 2P threads split the work: threads 0..P-1 rows, P..2P-1 columns.
+    // overflows float32 (entries near the float32 limit) is redone in float64.  Multi-warp
+    // teams split the work: threads 0..P-1 rows, P..2P-1 columns.
     auto line_sum = [&](int l, bool column) {
       // element k of line l: a[l][k] for a row, a[k][l] for a column
       auto at = [&](int k) { return team[column ? pidx<P, TM>(k, l) : pidx<P, TM>(l, k)]; };
@@ -553,7 +586,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     };
     static_assert(T <= 32 || (P == 32 && T >= 2 * P), "team norm split");
     double nrow = 0.0, ncol = 0.0;
-    if constexpr (T >= 2 * P) {
+    if constexpr (T > 32) {
       if (t < P) {
         nrow = line_sum(t, false);
       } else if (t < 2 * P) {
