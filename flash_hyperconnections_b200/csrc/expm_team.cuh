@@ -1,32 +1,33 @@
 // Team kernel: padded sizes P = 8, 16, 32 (n = 5..32).
 //
 // A "team" of T = (P/TM) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
-// the TM x TN register tile at rows TM*rb.., columns TN*cb...  TN = 8 or 4 per configuration,
-// so a team is 2..32 lanes of one warp or, for the 32 x 32 Frechet derivative, two warps.
-// The matrix state lives in five shared-memory plane slots per team; registers hold only
-// the accumulator tile of the product in flight.
+// the TM x TN register tile at rows TM*rb.., columns TN*cb...  Teams of 4 or 16 threads share
+// a warp (P = 8, 16); at P = 32 a team is two warps (forward, 4 x 4 tiles) or four warps
+// (Frechet, 2 x 4 tiles).  The matrix state lives in five shared-memory plane slots per team;
+// registers hold only the accumulator tile of the product in flight.
 //
 // Every polynomial step and every squaring is one product R = X Y (+ Z) of slots X, Y (Z an
 // optional slot added on the way in), computed as a register-tiled outer product: per four
-// k a thread reads the 4 x 4 block of X it needs (four 128-bit loads) and per k the TN
-// values of row k of Y (TN/4 128-bit loads) for 4 TN FMAs -- three times that in Frechet
-// mode, where every matrix is the pair (M, dM) of the block-triangular [[M, dM], [0, M]] and
-// (X, dX)(Y, dY) = (XY, X dY + dX Y).  Planes are row-major with the 16-byte chunks of row i
-// rotated by i/4, so the block reads of different row blocks hit different bank groups while
-// every chunk stays 16-byte aligned.
+// k a thread reads the TM x 4 block of X it needs (TM 128-bit loads) and per k the TN values
+// of row k of Y (TN/4 128-bit loads), accumulating in float2 pairs with the paired FMA of
+// sm_100 (FFMA2) -- three products at once in Frechet mode, where every matrix is the pair
+// (M, dM) of the block-triangular [[M, dM], [0, M]] and (X, dX)(Y, dY) = (XY, X dY + dX Y).
+// Planes are row-major with the 16-byte chunks of row i rotated by i/4, so the block reads of
+// different row blocks hit different bank groups while every chunk stays 16-byte aligned.
 //
-// The degree-m schemes are table-driven "step programs" (kSteps below): after each product
-// the thread writes R into a slot and applies a short list of element-wise linear
-// combinations to its own tile (the next operands of the scheme).  Teams sharing a warp run
-// the product loop in lockstep with a barrier after the product and after the epilogue; a
-// team whose program (pi(m) + s steps) is shorter idles, so every matrix is computed with
-// exactly its own (m, s) and its result never depends on its neighbours.  The code is kept
-// compact on purpose: a fully unrolled per-degree epilogue overflows the instruction cache
-// (measured: instruction-fetch stalls dominated an earlier unrolled version).
+// The degree-m schemes are table-driven "step programs" (step_def below): after each product
+// the thread writes R into a slot and applies the step's element-wise linear combinations to
+// its own tile (the next operands of the scheme), with the coefficients as compile-time
+// immediates.  Multi-warp teams synchronise with a named barrier per team and square in
+// ping-pong between two slots (one barrier per squaring).  Teams that share a warp run in
+// lockstep with __syncwarp and one program: the largest degree chosen in the warp, each
+// matrix keeping its own number of squarings (a higher degree with the same scaling is at
+// least as accurate), so that the step epilogues of different degrees never run one after
+// another inside a warp.
 //
-// Loads and stores are line-per-thread: thread t of a team moves rows t, t + T, ... of the
-// matrix between global memory (any strides, three dtypes) and slot 0, accumulating the row
-// sums of |A| on the way; the column sums are read back from the slot.
+// Loads are 16-byte chunks spread over the team and prefetched one matrix ahead into
+// registers as raw bits (decoded when the next matrix starts); norms are read back from the
+// slot; results leave in 16-byte chunks.
 //
 // Work is persistent: grid = resident CTAs, CTA c takes CTA items c, c + gridDim.x, ...
 //
@@ -259,7 +260,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
 #pragma unroll
       for (int jj = 0; jj < TN / 2; ++jj) V[ii][jj] = make_float2(0.f, 0.f);
   }
-#pragma unroll(Pair ? 1 : 2)
+#pragma unroll(Pair ? (P == 32 ? 2 : 1) : (P == 32 ? 4 : 2))
   for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
     const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
     float4 xb[TM], xub[TM];
@@ -401,10 +402,9 @@ __device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, 
   }
 }
 
-// The steps that have outputs, dispatched on the runtime step index.  Kept out of line:
-// only one or two of them run per matrix, and the step loop stays compact.
+// The steps that have outputs, dispatched on the runtime step index.
 template <int P, int TM, int TN, bool Pair>
-__device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+__device__ __forceinline__ void team_epilogue_inline(int step_index, float* __restrict__ team, int i0, int j0) {
   switch (step_index) {
 #define FHX_EPI(S)                                                                           \
   case S:                                                                                    \
@@ -415,6 +415,22 @@ __device__ __noinline__ void team_epilogue(int step_index, float* __restrict__ t
 #undef FHX_EPI
     default:
       break;
+  }
+}
+
+// Out of line for the 32 x 32 forward kernel (measured faster: its step loop stays compact);
+// inline elsewhere (measured faster: no call-boundary register traffic).
+template <int P, int TM, int TN, bool Pair>
+__device__ __noinline__ void team_epilogue_call(int step_index, float* __restrict__ team, int i0, int j0) {
+  team_epilogue_inline<P, TM, TN, Pair>(step_index, team, i0, j0);
+}
+
+template <int P, int TM, int TN, bool Pair>
+__device__ __forceinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+  if constexpr (P == 32 && !Pair) {
+    team_epilogue_call<P, TM, TN, Pair>(step_index, team, i0, j0);
+  } else {
+    team_epilogue_inline<P, TM, TN, Pair>(step_index, team, i0, j0);
   }
 }
 
@@ -588,7 +604,18 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     double nrow = 0.0, ncol = 0.0;
     if constexpr (T > 32) {
       if (t < P) {
-        nrow = line_sum(t, false);
+        // row t with 128-bit loads; same partial sums (element k into ps[k % 4], k ascending)
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c4 = 0; c4 < P / 4; ++c4) {
+          const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(t, 4 * c4));
+          ps[0] += fabsf(x.x);
+          ps[1] += fabsf(x.y);
+          ps[2] += fabsf(x.z);
+          ps[3] += fabsf(x.w);
+        }
+        nrow = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
+        if (!isfinite(nrow)) nrow = line_sum(t, false);
       } else if (t < 2 * P) {
         ncol = line_sum(t - P, true);
       }
