@@ -252,14 +252,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   const unsigned c016 = unsigned(j0 >> 2) << 4;  // first column chunk of the tile (bytes)
   const unsigned xrow = smem_addr(X) + unsigned(i0) * ROW_B;
   unsigned yrow = smem_addr(Y);
-  // Frechet: R.u accumulates X dY, V accumulates dX Y (independent FMA chains).
-  float2 V[Pair ? TM : 1][Pair ? TN / 2 : 1];
-  if constexpr (Pair) {
-#pragma unroll
-    for (int ii = 0; ii < TM; ++ii)
-#pragma unroll
-      for (int jj = 0; jj < TN / 2; ++jj) V[ii][jj] = make_float2(0.f, 0.f);
-  }
+  // Frechet: R.u accumulates X dY and dX Y, interleaved per k.
 #pragma unroll(Pair ? (P == 32 ? 2 : 1) : (P == 32 ? 4 : 2))
   for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
     const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
@@ -297,25 +290,19 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
           R.d[ii][jj] = __ffma2_rn(x2, y[jj], R.d[ii][jj]);
           if constexpr (Pair) {
             R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
-            V[ii][jj] = __ffma2_rn(xu2, y[jj], V[ii][jj]);
+            R.u[ii][jj] = __ffma2_rn(xu2, y[jj], R.u[ii][jj]);
           }
         }
       }
     }
     yrow += 4u * ROW_B;
   }
-  if constexpr (Pair) {
-#pragma unroll
-    for (int ii = 0; ii < TM; ++ii)
-#pragma unroll
-      for (int jj = 0; jj < TN / 2; ++jj) R.u[ii][jj] = __fadd2_rn(R.u[ii][jj], V[ii][jj]);
-  }
 }
 
 // Element-wise linear combinations of step S on the thread's own TM x TN tile, with the
 // coefficients of step_def(S) as compile-time constants: zero terms vanish, and each term is
-// one FFMA with an immediate coefficient.  Terms are accumulated in the table's order,
-// identity first.
+// one FMA per element with an immediate coefficient (paired FMAs at P <= 16).  Terms are
+// accumulated in the table's order, identity first.
 template <int P, int TM, int TN, bool Pair, int S>
 __device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, int j0) {
   constexpr Step st = step_def(S);
