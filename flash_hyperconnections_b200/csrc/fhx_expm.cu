@@ -124,9 +124,9 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   }
   // Tile shapes (TM x TN per thread) and warps per team, chosen by measurement on B200:
   // more warps per SM beat larger per-thread tiles as long as the shared-memory wavefront
-  // budget holds.  32 x 32: forward 4 x 4 tiles in two-warp teams, Frechet 2 x 4 tiles in
-  // four-warp teams (20 warps per SM at 40 KB of shared state per matrix).  8 x 8 and
-  // 16 x 16: 4 x 4 tiles, several teams per warp.
+  // budget holds.  32 x 32: forward 4 x 4 tiles in two-warp teams (16 warps per SM at 128
+  // registers), Frechet 2 x 4 tiles in four-warp teams (20 warps per SM at 40 KB of shared
+  // state per matrix).  8 x 8 and 16 x 16: 4 x 4 tiles, several teams per warp.
   if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, batch, n, dtype, stream);
   if (n <= 16) return launch_team<16, 4, 4, Pair, 1>(a, e, out, batch, n, dtype, stream);
   if constexpr (Pair) {
