@@ -8,12 +8,24 @@
 // contiguous output (csrc/matrix_exp.cu:68) under a device guard (:60) and launch on the
 // current stream (:16).  Instead of materialising padded FP32 copies (:35-44), they pass the
 // input's strides and lazy negation bit straight to the C ABI.
+//
+// The autograd formula of _matrix_exp is registered here, in C++, with the behaviour of the
+// reference's Python registration (flash_hypercons/ops/matrix_exp/__init__.py:61-77): the input
+// is saved; the backward is _frechet(input.mT, grad) -- or, when a graph of the backward itself
+// is needed (grad mode on, or a forward-mode tangent on the input or the incoming gradient), the
+// differentiable float32 block formula exp([[A^T, G], [0, A^T]]) of native operators
+// (__init__.py:32-37).  Kept in C++ because the Python autograd wrapper cost about 60 us per
+// forward + backward, which dominated small batches.
 #include <Python.h>
 
 #include <ATen/core/Tensor.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/ops/cat.h>
 #include <ATen/ops/empty.h>
+#include <ATen/ops/linalg_matrix_exp.h>
+#include <ATen/ops/zeros_like.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <torch/csrc/autograd/custom_function.h>
 #include <torch/library.h>
 
 #include "fhx.h"
@@ -67,6 +79,49 @@ at::Tensor matrix_exp_cuda(const at::Tensor& input) { return run(input, nullptr)
 
 at::Tensor frechet_cuda(const at::Tensor& input, const at::Tensor& direction) { return run(input, &direction); }
 
+// Differentiable L(input, direction): the upper-right block of the native exponential of
+// [[A, E], [0, A]] in float32, cast back (reference __init__.py:32-37).
+at::Tensor frechet_reference(const at::Tensor& input, const at::Tensor& direction) {
+  const int64_t n = input.size(-1);
+  const at::Tensor a = input.to(at::kFloat);
+  const at::Tensor e = direction.to(at::kFloat);
+  const at::Tensor top = at::cat({a, e}, -1);
+  const at::Tensor bottom = at::cat({at::zeros_like(a), a}, -1);
+  return at::linalg_matrix_exp(at::cat({top, bottom}, -2)).slice(-2, 0, n).slice(-1, n, 2 * n).to(input.scalar_type());
+}
+
+bool has_tangent(const at::Tensor& t) { return t.defined() && t._fw_grad(/*level=*/0).defined(); }
+
+struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
+  static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& input) {
+    static const auto op = c10::Dispatcher::singleton()
+                               .findSchemaOrThrow("flash_hypercons::_matrix_exp", "")
+                               .typed<at::Tensor(const at::Tensor&)>();
+    at::Tensor out;
+    {
+      at::AutoDispatchBelowADInplaceOrView below;
+      out = op.call(input);
+    }
+    ctx->save_for_backward({input});
+    return out;
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    static const auto op = c10::Dispatcher::singleton()
+                               .findSchemaOrThrow("flash_hypercons::_frechet", "")
+                               .typed<at::Tensor(const at::Tensor&, const at::Tensor&)>();
+    const at::Tensor input = ctx->get_saved_variables()[0];
+    const at::Tensor& grad = grads[0];
+    if (at::GradMode::is_enabled() || has_tangent(input) || has_tangent(grad)) {
+      return {frechet_reference(input.mT(), grad)};
+    }
+    return {op.call(input.mT(), grad)};
+  }
+};
+
+at::Tensor matrix_exp_autograd(const at::Tensor& input) { return MatrixExpFunction::apply(input); }
+
 }  // namespace
 
 TORCH_LIBRARY(flash_hypercons, m) {
@@ -78,6 +133,8 @@ TORCH_LIBRARY_IMPL(flash_hypercons, CUDA, m) {
   m.impl("_matrix_exp", &matrix_exp_cuda);
   m.impl("_frechet", &frechet_cuda);
 }
+
+TORCH_LIBRARY_IMPL(flash_hypercons, Autograd, m) { m.impl("_matrix_exp", &matrix_exp_autograd); }
 
 static PyModuleDef module_def = {PyModuleDef_HEAD_INIT, "_C", "flash_hypercons operator registration", -1,
                                  nullptr};

@@ -1,15 +1,16 @@
-"""Python operator layer: eligibility, native routing, autograd, fake kernels, scoped routing.
+"""Python operator layer: eligibility, native routing, fake kernels, scoped routing.
 
 Behaviour mirrors flash_hypercons/ops/matrix_exp/__init__.py of the reference package
 (file:lines cited per function) so that code written against ``flash_hypercons`` runs
-unchanged.  The operators themselves are registered in C++ (``csrc/torch_ops.cpp``) and
-launch the sm_100a kernels of ``libfhx.so``.
+unchanged.  The operators and the autograd formula of ``_matrix_exp`` (the reference's
+``_setup_context`` / ``_backward`` / ``_frechet_reference``, __init__.py:32-37,61-77) are
+registered in C++ (``csrc/torch_ops.cpp``) and launch the sm_100a kernels of ``libfhx.so``.
 """
 
 from __future__ import annotations
 
 import torch
-from torch.overrides import TorchFunctionMode, has_torch_function
+from torch.overrides import TorchFunctionMode
 
 from ... import _C  # noqa: F401  (registers flash_hypercons::_matrix_exp / _frechet)
 
@@ -40,18 +41,6 @@ def _native(input: torch.Tensor, *, promote: bool = False) -> torch.Tensor:
     return _NATIVE(input)
 
 
-def _frechet_reference(input: torch.Tensor, direction: torch.Tensor) -> torch.Tensor:
-    """Differentiable L(input, direction) as the upper-right block of the native exponential of
-    [[A, E], [0, A]] in float32 (reference __init__.py:32-37); used when a graph of the
-    backward itself is needed."""
-    n = input.shape[-1]
-    a = input.float()
-    e = direction.float()
-    top = torch.cat((a, e), dim=-1)
-    bottom = torch.cat((torch.zeros_like(a), a), dim=-1)
-    return _NATIVE(torch.cat((top, bottom), dim=-2))[..., :n, n:].to(input.dtype)
-
-
 @torch.library.register_fake("flash_hypercons::_matrix_exp")
 def _matrix_exp_fake(input):
     # Same metadata checks as the reference fake (__init__.py:40-49).
@@ -75,39 +64,12 @@ def _frechet_fake(input, direction):
     return _matrix_exp_fake(input)
 
 
-def _setup_context(ctx, inputs, output):
-    # Only the input is kept; the backward recomputes the powers in-kernel
-    # (reference __init__.py:61-62).
-    ctx.save_for_backward(inputs[0])
-
-
 def _has_tangent(t) -> bool:
     # Outside every forward-AD level no tensor can carry a tangent; unpack_dual would
     # return None, so the (comparatively slow) call is skipped.
     if torch.autograd.forward_ad._current_level < 0:
         return False
     return torch.autograd.forward_ad.unpack_dual(t).tangent is not None
-
-
-def _needs_differentiable_backward(input, grad_output) -> bool:
-    return (
-        torch.is_grad_enabled()
-        or has_torch_function((input, grad_output))
-        or _has_tangent(input)
-        or _has_tangent(grad_output)
-    )
-
-
-def _backward(ctx, grad_output):
-    """dL/dA = L(A^T, dL/dY) (reference __init__.py:65-74).  ``input.mT`` is a strided view:
-    the kernel reads it through its swapped strides, no transposed copy is made."""
-    (input,) = ctx.saved_tensors
-    if _needs_differentiable_backward(input, grad_output):
-        return _frechet_reference(input.mT, grad_output)
-    return torch.ops.flash_hypercons._frechet(input.mT, grad_output)
-
-
-torch.library.register_autograd("flash_hypercons::_matrix_exp", _backward, setup_context=_setup_context)
 
 
 def matrix_exp(input: torch.Tensor) -> torch.Tensor:
