@@ -1,9 +1,9 @@
 // Team kernel: padded sizes P = 8, 16, 32 (n = 5..32).
 //
 // A "team" of T = (P/TM) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
-// the TM x TN register tile at rows TM*rb.., columns TN*cb...  Teams of 4 or 16 threads share
-// a warp (P = 8, 16); at P = 32 a team is two warps (forward, 4 x 4 tiles) or four warps
-// (Frechet, 2 x 4 tiles).  The matrix state lives in five shared-memory plane slots per team;
+// the TM x TN register tile at rows TM*rb.., columns TN*cb...  Teams of 4 threads (P = 8) or
+// 16 threads (P = 16 forward) share a warp; the P = 16 Frechet team is one warp (2 x 4 tiles);
+// at P = 32 a team is two warps (forward, 4 x 4 tiles) or four warps (Frechet, 2 x 4 tiles).  The matrix state lives in five shared-memory plane slots per team;
 // registers hold only the accumulator tile of the product in flight.
 //
 // Every polynomial step and every squaring is one product R = X Y (+ Z) of slots X, Y (Z an
@@ -617,9 +617,10 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     }
     int m = 1, s = 0, nsteps = 0;
     if constexpr (T <= 32) {
-      constexpr int RED = T < P ? T : P;  // threads 0 .. RED-1 of the team hold norms
+      // Max over all T lanes of the team: every lane must end with the team's (m, s).  Lanes
+      // t >= P (teams wider than the matrix) hold no line and contribute 0.
 #pragma unroll
-      for (int off = 1; off < RED; off <<= 1) {
+      for (int off = 1; off < T; off <<= 1) {
         nrow = fmax(nrow, __shfl_xor_sync(0xffffffffu, nrow, off));
         ncol = fmax(ncol, __shfl_xor_sync(0xffffffffu, ncol, off));
       }

@@ -126,9 +126,17 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   // more warps per SM beat larger per-thread tiles as long as the shared-memory wavefront
   // budget holds.  32 x 32: forward 4 x 4 tiles in two-warp teams (16 warps per SM at 128
   // registers), Frechet 2 x 4 tiles in four-warp teams (20 warps per SM at 40 KB of shared
-  // state per matrix).  8 x 8 and 16 x 16: 4 x 4 tiles, several teams per warp.
+  // state per matrix).  8 x 8: 4 x 4 tiles, eight teams per warp.  16 x 16: forward 4 x 4 tiles,
+  // two teams per warp; Frechet 2 x 4 tiles, one team per warp (20 % faster than 4 x 4 tiles,
+  // whose 254 registers left 8 warps per SM).
   if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, batch, n, dtype, stream);
-  if (n <= 16) return launch_team<16, 4, 4, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  if (n <= 16) {
+    if constexpr (Pair) {
+      return launch_team<16, 2, 4, true, 1>(a, e, out, batch, n, dtype, stream);
+    } else {
+      return launch_team<16, 4, 4, false, 1>(a, e, out, batch, n, dtype, stream);
+    }
+  }
   if constexpr (Pair) {
     return launch_team<32, 2, 4, true, 4>(a, e, out, batch, n, dtype, stream);
   } else {

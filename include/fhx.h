@@ -58,9 +58,9 @@ int32_t fhx_matrix_exp(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
  * exp([[A, E], [0, A]])).  The autograd backward of Y = exp(X) is
  * fhx_frechet(X^T, dY), obtained by passing X's strides with in_s1/in_s2 swapped.
  * The number of squarings depends on A only and is identical for A and A^T.  The Taylor
- * degree does too for n <= 4 and 17 <= n <= 32; for 5 <= n <= 16 a matrix runs the largest
- * degree chosen in its aligned group of 8 (n <= 8) or 2 (n <= 16) consecutive matrices, which
- * is at least as accurate.  Either way the backward repeats the forward's choice.
+ * degree does too, except where several matrices share a warp: for 5 <= n <= 8 (both entry
+ * points) and for the forward at 9 <= n <= 16, a matrix runs the largest degree chosen in its
+ * aligned group of 8 or 2 consecutive matrices, which is at least as accurate.
  * Any non-finite entry of A or E makes that matrix's whole output NaN.
  */
 int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
