@@ -38,6 +38,12 @@ __device__ __forceinline__ float4 ld_f32x4(const float* p) {
   return v;
 }
 
+__device__ __forceinline__ uint2 ld_u32x2(const unsigned* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t off) {
   if (dtype == kF32) return ld_f32(static_cast<const float*>(p) + off);
   const unsigned short raw = ld_u16(static_cast<const unsigned short*>(p) + off);

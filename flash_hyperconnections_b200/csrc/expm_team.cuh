@@ -45,12 +45,13 @@ constexpr int kSlots = 5;
 // Layout flags of a launch (computed on the host from strides, dtype and alignment).
 // A view is moved in 16-byte chunks: four consecutive elements of a row ("row chunks",
 // when the elements of a row are closest in memory, s2 <= s1) or of a column ("column
-// chunks", s1 < s2).  "Vec": float32, the chunk contiguous and 16-byte aligned, n == P.
+// chunks", s1 < s2).  "Vec": the chunk is contiguous and aligned (16 bytes for float32, 8 for
+// the half types) and n == P, so it is one 128-bit or 64-bit load.
 enum : unsigned {
   kARows = 1u,    // input: row chunks
-  kAVec = 2u,     // input: one 128-bit load per chunk
+  kAVec = 2u,     // input: one vector load per chunk
   kERows = 4u,    // direction: row chunks
-  kEVec = 8u,     // direction: one 128-bit load per chunk
+  kEVec = 8u,     // direction: one vector load per chunk
   kOutVec = 16u,  // output: n % 4 == 0 and 16-byte (float32) / 8-byte (half types) aligned
 };
 constexpr int kMaxIn = 4;
@@ -429,8 +430,13 @@ __device__ __forceinline__ uint4 load_chunk_raw(const View& v, int dtype, int64_
                                                 bool vec) {
   const int64_t base = b * v.s0 + int64_t(r) * v.s1 + int64_t(c) * v.s2;
   if (vec) {
-    const float4 x = ld_f32x4(static_cast<const float*>(v.data) + base);
-    return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
+    if (dtype == kF32) {
+      const float4 x = ld_f32x4(static_cast<const float*>(v.data) + base);
+      return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
+    }
+    // four 16-bit elements in one 64-bit load, each moved to the low half of a word
+    const uint2 h = ld_u32x2(reinterpret_cast<const unsigned*>(static_cast<const unsigned short*>(v.data) + base));
+    return make_uint4(h.x & 0xffffu, h.x >> 16, h.y & 0xffffu, h.y >> 16);
   }
   const int64_t step = rowc ? v.s2 : v.s1;
   unsigned w[4];

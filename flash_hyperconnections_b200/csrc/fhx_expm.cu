@@ -74,12 +74,13 @@ template <int P>
 unsigned layout_flags(const View& a, const View& e, const void* out, int n, int dtype, bool pair) {
   unsigned f = 0;
   // Row chunks when the elements of a row are closest in memory, else column chunks; a chunk
-  // is one 128-bit load when it is contiguous, 16-byte aligned, float32 and n == P.
+  // is one 128-bit (float32) or 64-bit (half types) load when it is contiguous, aligned and
+  // n == P.
   auto rows = [](const View& v) { return v.s2 <= v.s1; };
   auto vec = [&](const View& v) {
     const int64_t inner = rows(v) ? v.s2 : v.s1;
     const int64_t outer = rows(v) ? v.s1 : v.s2;
-    return dtype == kF32 && n == P && inner == 1 && outer % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, 16);
+    return n == P && inner == 1 && outer % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, dtype == kF32 ? 16 : 8);
   };
   if (rows(a)) f |= kARows;
   if (vec(a)) f |= kAVec;
