@@ -690,8 +690,8 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
           }
       }
     }
-    team_sync<T>(tic);
-    if (t == 0) scratch[3] = 0;  // non-finite flag: every thread has read it; free for the next matrix
+    // Multi-warp teams skip this barrier when nothing was rescaled (team-uniform condition).
+    if (T <= 32 || s > 0 || m == 1) team_sync<T>(tic);
 
     // ---- polynomial steps, then squarings ----
     // Whole-warp teams square in ping-pong between slots 0 and 1: the slot written in a
@@ -768,6 +768,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
         }
       }
     }
+    if (t == 0) scratch[3] = 0;  // non-finite flag: every thread read it before the steps
     team_sync<T>(tic);  // the result slot is read before the next matrix is written
   }
 }
