@@ -284,15 +284,21 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
       for (int ii = 0; ii < TM; ++ii) {
         const float x = f4get(xb[ii], r);
         const float2 x2 = make_float2(x, x);
-        float2 xu2 = make_float2(0.f, 0.f);
-        if constexpr (Pair) xu2 = make_float2(f4get(xub[ii], r), f4get(xub[ii], r));
 #pragma unroll
         for (int jj = 0; jj < TN / 2; ++jj) {
           R.d[ii][jj] = __ffma2_rn(x2, y[jj], R.d[ii][jj]);
-          if constexpr (Pair) {
-            R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
-            R.u[ii][jj] = __ffma2_rn(xu2, y[jj], R.u[ii][jj]);
-          }
+          if constexpr (Pair) R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
+        }
+      }
+      if constexpr (Pair) {
+        // second derivative term after every other FMA of this k: the two updates of R.u are
+        // a whole pass apart
+#pragma unroll
+        for (int ii = 0; ii < TM; ++ii) {
+          const float xu = f4get(xub[ii], r);
+          const float2 xu2 = make_float2(xu, xu);
+#pragma unroll
+          for (int jj = 0; jj < TN / 2; ++jj) R.u[ii][jj] = __ffma2_rn(xu2, y[jj], R.u[ii][jj]);
         }
       }
     }
