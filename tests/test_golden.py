@@ -52,3 +52,22 @@ def test_float64_truth_against_reference_kernels(golden, n, name):
     kind = "float32" if name == "float32" else "half"
     assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance(kind, False)
     assert O.per_matrix_error(l, O.frechet_fp64(a, e)).max() <= O.tolerance(kind, True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(DTYPES))
+@pytest.mark.parametrize("n", SIZES)
+def test_kernels_against_reference_kernels(golden, n, name):
+    """This package's operators on the golden inputs agree with the reference kernels' outputs
+    within the reference's per-matrix tolerance."""
+    import flash_hypercons  # noqa: F401  (registers the operators)
+
+    key = f"n{n}_{name}"
+    a, e, y, l = (golden[f"{key}_{t}"] for t in "AEYL")
+    at = torch.from_numpy(a).to(DTYPES[name]).cuda()
+    et = torch.from_numpy(e).to(DTYPES[name]).cuda()
+    ours_y = torch.ops.flash_hypercons._matrix_exp(at).float().cpu().numpy()
+    ours_l = torch.ops.flash_hypercons._frechet(at, et).float().cpu().numpy()
+    kind = "float32" if name == "float32" else "half"
+    assert O.per_matrix_error(ours_y, y).max() <= O.tolerance(kind, False)
+    assert O.per_matrix_error(ours_l, l).max() <= O.tolerance(kind, True)
