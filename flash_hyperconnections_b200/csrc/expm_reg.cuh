@@ -165,9 +165,26 @@ __device__ __forceinline__ RMat<N, Pair> taylor(int m, const RMat<N, Pair>& a) {
   return r;
 }
 
+// Row i of matrix b of a view as four elements (N == 4, row contiguous and aligned): one
+// 128-bit (float32) or 64-bit (half types) load.
+__device__ __forceinline__ float4 load_row4(const View& v, int dtype, int64_t off) {
+  if (dtype == kF32) {
+    const float4 x = ld_f32x4(static_cast<const float*>(v.data) + off);
+    return make_float4(v.sign * x.x, v.sign * x.y, v.sign * x.z, v.sign * x.w);
+  }
+  const uint2 h = ld_u32x2(reinterpret_cast<const unsigned*>(static_cast<const unsigned short*>(v.data) + off));
+  auto dec = [&](unsigned w) {
+    const unsigned short u = static_cast<unsigned short>(w);
+    return v.sign * (dtype == kBF16 ? __bfloat162float(__ushort_as_bfloat16(u)) : __half2float(__ushort_as_half(u)));
+  };
+  return make_float4(dec(h.x & 0xffffu), dec(h.x >> 16), dec(h.y & 0xffffu), dec(h.y >> 16));
+}
+
+// flags: bit 0 = rows of A are one vector load each, bit 1 = same for E, bit 2 = output rows
+// can be stored as one vector each (N == 4 only).
 template <int N, bool Pair>
 __global__ void __launch_bounds__(128) expm_reg_kernel(View a, View e, void* __restrict__ out, int64_t batch,
-                                                       int dtype) {
+                                                       int dtype, unsigned flags) {
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   RMat<N, Pair> x;
@@ -179,18 +196,42 @@ __global__ void __launch_bounds__(128) expm_reg_kernel(View a, View e, void* __r
   const int64_t ebase = b * e.s0;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
+    float va[N], ve[N];
+    if constexpr (N == 4) {
+      if (flags & 1u) {
+        const float4 r4 = load_row4(a, dtype, abase + i * a.s1);
+        va[0] = r4.x; va[1] = r4.y; va[2] = r4.z; va[3] = r4.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j) va[j] = a.sign * load_elem(a.data, dtype, abase + i * a.s1 + j * a.s2);
+      }
+      if constexpr (Pair) {
+        if (flags & 2u) {
+          const float4 r4 = load_row4(e, dtype, ebase + i * e.s1);
+          ve[0] = r4.x; ve[1] = r4.y; ve[2] = r4.z; ve[3] = r4.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < N; ++j) ve[j] = e.sign * load_elem(e.data, dtype, ebase + i * e.s1 + j * e.s2);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        va[j] = a.sign * load_elem(a.data, dtype, abase + i * a.s1 + j * a.s2);
+        if constexpr (Pair) ve[j] = e.sign * load_elem(e.data, dtype, ebase + i * e.s1 + j * e.s2);
+      }
+    }
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      const float v = a.sign * load_elem(a.data, dtype, abase + i * a.s1 + j * a.s2);
+      const float v = va[j];
       x.d[i * N + j] = v;
       bad |= !isfinite(v);
       const double av = fabs(double(v));
       col[j] += av;
       row[i] += av;
       if constexpr (Pair) {
-        const float w = e.sign * load_elem(e.data, dtype, ebase + i * e.s1 + j * e.s2);
-        x.u[i * N + j] = w;
-        bad |= !isfinite(w);
+        x.u[i * N + j] = ve[j];
+        bad |= !isfinite(ve[j]);
       }
     }
   }
@@ -217,14 +258,16 @@ __global__ void __launch_bounds__(128) expm_reg_kernel(View a, View e, void* __r
   }
   RMat<N, Pair> r = taylor<N, Pair>(m, x);
   for (int t = 0; t < s; ++t) r = rmul(r, r);
+  const float* res = Pair ? r.u : r.d;
+  if constexpr (N == 4) {
+    if (flags & 4u) {
 #pragma unroll
-  for (int t = 0; t < N * N; ++t) {
-    if constexpr (Pair) {
-      store_elem(out, dtype, obase + t, r.u[t]);
-    } else {
-      store_elem(out, dtype, obase + t, r.d[t]);
+      for (int i = 0; i < N; ++i) store_chunk(out, dtype, obase + 4 * i, make_float4(res[4 * i], res[4 * i + 1], res[4 * i + 2], res[4 * i + 3]));
+      return;
     }
   }
+#pragma unroll
+  for (int t = 0; t < N * N; ++t) store_elem(out, dtype, obase + t, res[t]);
 }
 
 }  // namespace fhx

@@ -58,16 +58,26 @@ int resident_blocks(Kernel kernel, LaunchShape& shape, int dev, int threads, siz
   return shape.blocks_per_sm[dev];
 }
 
+bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
+
 template <int N, bool Pair>
 int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype, cudaStream_t stream) {
   constexpr int threads = 128;
   const int64_t blocks = (batch + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
-  expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, batch, dtype);
+  // 4 x 4: rows with unit inner stride, 4-element-aligned row and matrix strides and an aligned
+  // base are read as one vector each; the contiguous output is written the same way.
+  const size_t row_bytes = dtype == kF32 ? 16 : 8;
+  auto rows = [&](const View& v) {
+    return N == 4 && v.s2 == 1 && v.s1 % 4 == 0 && v.s0 % 4 == 0 && aligned(v.data, row_bytes);
+  };
+  unsigned flags = 0;
+  if (rows(a)) flags |= 1u;
+  if (Pair && rows(e)) flags |= 2u;
+  if (N == 4 && aligned(out, row_bytes)) flags |= 4u;
+  expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, batch, dtype, flags);
   return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
 }
-
-bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
 
 // Load/store layout flags of the team kernel (see the enum in expm_team.cuh).
 template <int P>
