@@ -25,22 +25,49 @@ struct RMat {
 template <int N, bool Pair>
 __device__ __forceinline__ RMat<N, Pair> rmul(const RMat<N, Pair>& x, const RMat<N, Pair>& y) {
   RMat<N, Pair> r;
+  if constexpr (N % 2 == 0) {
+    // pairs of adjacent columns with one paired FMA (FFMA2) each
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
+    for (int i = 0; i < N; ++i) {
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      float acc = 0.f;
-      float accu = 0.f;
+      for (int j = 0; j < N; j += 2) {
+        float2 acc = make_float2(0.f, 0.f), accu = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < N; ++k) {
-        acc = fmaf(x.d[i * N + k], y.d[k * N + j], acc);
+        for (int k = 0; k < N; ++k) {
+          const float2 xd = make_float2(x.d[i * N + k], x.d[i * N + k]);
+          const float2 yd = make_float2(y.d[k * N + j], y.d[k * N + j + 1]);
+          acc = __ffma2_rn(xd, yd, acc);
+          if constexpr (Pair) {
+            accu = __ffma2_rn(xd, make_float2(y.u[k * N + j], y.u[k * N + j + 1]), accu);
+            accu = __ffma2_rn(make_float2(x.u[i * N + k], x.u[i * N + k]), yd, accu);
+          }
+        }
+        r.d[i * N + j] = acc.x;
+        r.d[i * N + j + 1] = acc.y;
         if constexpr (Pair) {
-          accu = fmaf(x.d[i * N + k], y.u[k * N + j], accu);
-          accu = fmaf(x.u[i * N + k], y.d[k * N + j], accu);
+          r.u[i * N + j] = accu.x;
+          r.u[i * N + j + 1] = accu.y;
         }
       }
-      r.d[i * N + j] = acc;
-      if constexpr (Pair) r.u[i * N + j] = accu;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float acc = 0.f;
+        float accu = 0.f;
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+          acc = fmaf(x.d[i * N + k], y.d[k * N + j], acc);
+          if constexpr (Pair) {
+            accu = fmaf(x.d[i * N + k], y.u[k * N + j], accu);
+            accu = fmaf(x.u[i * N + k], y.d[k * N + j], accu);
+          }
+        }
+        r.d[i * N + j] = acc;
+        if constexpr (Pair) r.u[i * N + j] = accu;
+      }
     }
   }
   return r;
