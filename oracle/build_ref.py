@@ -21,7 +21,8 @@ import subprocess
 import sys
 import sysconfig
 
-REF = pathlib.Path(os.environ.get("FHX_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: $FHX_REFERENCE_ROOT, else a "reference" directory beside this repository.
+REF = pathlib.Path(os.environ.get("FHX_REFERENCE_ROOT", pathlib.Path(__file__).resolve().parents[2] / "reference"))
 OUT_DIR = pathlib.Path(__file__).resolve().parent / "_ref"
 OUT = OUT_DIR / "flash_hypercons_ref.so"
 CUDA_HOME = pathlib.Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
