@@ -88,6 +88,14 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_ints(self, values: list[int]) -> list[int]:
+        if self.pg is None:
+            return list(values)
+        device = f"cuda:{self.local_rank}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor(values, dtype=torch.int64, device=device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return [int(v) for v in t.tolist()]
+
     def close(self):
         if self.pg is not None:
             self.pg.destroy_process_group()
@@ -220,6 +228,19 @@ E2E_CHUNK = 8192
 E2E_STREAMS = 4
 
 
+def result_digest(fh, a, g) -> list[int]:
+    """Integer sums of the raw bits of Y and of the gradient of this rank's shard (one more step,
+    after the timed region).  Summed over ranks they give a whole-batch digest that must be the same
+    at every GPU count: the shards are generated identically and no matrix depends on another."""
+    y, grad = fwd_bwd(fh, a, g)
+    out = []
+    for t in (y.detach(), grad):
+        bits = t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32)
+        out.append(int(bits.to(torch.int64).sum().item()))
+    del y, grad
+    return out
+
+
 def e2e_steps(fh, cfg, a_host, g_host, steps: int, warmup: int, dist: Dist, device,
               chunk: int = E2E_CHUNK, nstreams: int = E2E_STREAMS):
     """Same metric through the public API from pinned host buffers: every step copies its
@@ -309,7 +330,9 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         flush = torch.empty(64 * 2**20, dtype=torch.float32, device=device)
     launches = count_our_launches(fh, a, g)
     total_ms, fwd_ms, bwd_ms = time_steps(fh, a, g, steps, warmup, dist, flush)
+    digest = result_digest(fh, a, g)
     result = {
+        "digest": digest,
         "count": count,
         "total_ms": total_ms,
         "fwd_ms": fwd_ms,
@@ -420,6 +443,7 @@ def main():
                               with_e2e=not args.no_extras, batch=args.batch)
     clocks = sampler.stop() if sampler else None
 
+    digest = dist.sum_ints(main_res["digest"])
     total_ms = dist.max(main_res["total_ms"])
     fwd_ms = dist.max(main_res["fwd_ms"])
     bwd_ms = dist.max(main_res["bwd_ms"])
@@ -497,6 +521,8 @@ def main():
                        "no collective", "l2": main_res["l2"],
                        "mean_products_per_matrix": main_res["mean_steps"]},
             "gpu_launches": main_res["launches_per_step"] * args.steps,
+            "result_digest": {"y_bits_sum": digest[0], "grad_bits_sum": digest[1],
+                              "note": "sum over ranks of the raw bits of Y and the gradient; the same at every GPU count"},
             "kernel_ms": {"fwd": fwd_ms / 1.0, "bwd": bwd_ms / 1.0},
             "roofline": roofline,
             "clocks": clocks,
