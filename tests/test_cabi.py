@@ -77,20 +77,23 @@ def _call(lib, a, out, e=None, stream=None):
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("n", [2, 3, 4, 5, 8, 12, 16, 17, 31, 32])
-@pytest.mark.parametrize("layout", ["contiguous", "transposed", "strided", "expanded"])
+@pytest.mark.parametrize("layout", ["contiguous", "transposed", "strided", "expanded", "offset"])
 def test_cabi_parity_with_guard_bands(dtype, n, layout):
     lib = _native.load_cabi()
     batch = 37
-    base = torch.randn(batch, n + 3, n + 5, device="cuda") * 0.3
+    base = (torch.randn(batch, n + 3, n + 5, device="cuda") * 0.3).to(dtype)  # views keep their strides
     if layout == "contiguous":
         a = base[:, :n, :n].contiguous()
     elif layout == "transposed":
         a = base[:, :n, :n].contiguous().mT
     elif layout == "strided":
         a = base[:, 1 : n + 1, 2 : n + 2]
-    else:
+    elif layout == "expanded":
         a = base[:1, :n, :n].expand(batch, n, n)
-    a = a.to(dtype) if dtype != torch.float32 else a
+    else:  # contiguous strides, base address one element past an aligned boundary
+        flat = torch.empty(batch * n * n + 1, device="cuda", dtype=dtype)
+        a = flat[1:].view(batch, n, n)
+        a.copy_(base[:, :n, :n])
     e = (torch.randn(batch, n, n, device="cuda") * 0.5).to(dtype)
     guard = 64
     for direction in (None, e):
