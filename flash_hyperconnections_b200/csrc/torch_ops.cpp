@@ -9,13 +9,15 @@
 // current stream (:16).  Instead of materialising padded FP32 copies (:35-44), they pass the
 // input's strides and lazy negation bit straight to the C ABI.
 //
-// The autograd formula of _matrix_exp is registered here, in C++, with the behaviour of the
-// reference's Python registration (flash_hypercons/ops/matrix_exp/__init__.py:61-77): the input
-// is saved; the backward is _frechet(input.mT, grad) -- or, when a graph of the backward itself
-// is needed (grad mode on, or a forward-mode tangent on the input or the incoming gradient), the
-// differentiable float32 block formula exp([[A^T, G], [0, A^T]]) of native operators
-// (__init__.py:32-37).  Kept in C++ because the Python autograd wrapper cost about 60 us per
-// forward + backward, which dominated small batches.
+// The autograd formula of _matrix_exp is registered here, in C++ (the reference registers it from
+// Python, flash_hypercons/ops/matrix_exp/__init__.py:61-77): the input is saved and the backward
+// is _frechet(input.mT, grad).  With a forward-mode tangent on the input or the incoming gradient
+// it is the differentiable float32 block formula exp([[A^T, G], [0, A^T]]) of native operators
+// (__init__.py:32-37), as in the reference.  When a graph of the backward is built (grad mode on),
+// the reference also takes that native formula; here _frechet itself carries an autograd
+// formula, so second derivatives run through the kernels too (2n <= 32 for the second-order
+// term).  Kept in C++ because the Python autograd wrapper cost about 60 us per forward +
+// backward, which dominated small batches.
 #include <Python.h>
 
 #include <ATen/core/Tensor.h>
@@ -92,6 +94,63 @@ at::Tensor frechet_reference(const at::Tensor& input, const at::Tensor& directio
 
 bool has_tangent(const at::Tensor& t) { return t.defined() && t._fw_grad(/*level=*/0).defined(); }
 
+const auto& frechet_op() {
+  static const auto op = c10::Dispatcher::singleton()
+                             .findSchemaOrThrow("flash_hypercons::_frechet", "")
+                             .typed<at::Tensor(const at::Tensor&, const at::Tensor&)>();
+  return op;
+}
+
+// Second-order Frechet derivative D^2 exp(X)[E1, E2] as the upper-right block of
+// L(Z, W), Z = [[X, E1], [0, X]], W = [[E2, 0], [0, E2]] (d/dt of exp(Z + tW), whose upper-right
+// block is L(X + tE2, E1)).  The 2n x 2n matrices go through the Frechet kernel while 2n <= 32;
+// otherwise, or when a graph is needed, through the differentiable native block formula.
+at::Tensor frechet_second(const at::Tensor& x, const at::Tensor& e1, const at::Tensor& e2, bool differentiable) {
+  const int64_t n = x.size(-1);
+  const at::Tensor zero = at::zeros_like(x);
+  const at::Tensor z = at::cat({at::cat({x, e1}, -1), at::cat({zero, x}, -1)}, -2);
+  const at::Tensor w = at::cat({at::cat({e2, zero}, -1), at::cat({zero, e2}, -1)}, -2);
+  const at::Tensor l = (differentiable || 2 * n > FHX_MAX_N || !x.is_cuda()) ? frechet_reference(z, w)
+                                                                               : frechet_op().call(z, w);
+  return l.slice(-2, 0, n).slice(-1, n, 2 * n);
+}
+
+// Autograd formula of _frechet (used when a graph of the first backward is built): with
+// Y = L(X, E) and upstream gradient H, dX = D^2 exp(X^T)[E^T, H] and dE = L(X^T, H) (adjoints
+// of the first and second Frechet derivatives of exp).
+struct FrechetFunction : public torch::autograd::Function<FrechetFunction> {
+  static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& input,
+                            const at::Tensor& direction) {
+    at::Tensor out;
+    {
+      at::AutoDispatchBelowADInplaceOrView below;
+      out = frechet_op().call(input, direction);
+    }
+    ctx->save_for_backward({input, direction});
+    return out;
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    const auto saved = ctx->get_saved_variables();
+    const at::Tensor& input = saved[0];
+    const at::Tensor& direction = saved[1];
+    const at::Tensor& grad = grads[0];
+    const bool differentiable =
+        at::GradMode::is_enabled() || has_tangent(input) || has_tangent(direction) || has_tangent(grad);
+    at::Tensor d_input, d_direction;
+    if (ctx->needs_input_grad(0)) d_input = frechet_second(input.mT(), direction.mT(), grad, differentiable);
+    if (ctx->needs_input_grad(1)) {
+      d_direction = differentiable ? frechet_reference(input.mT(), grad) : frechet_op().call(input.mT(), grad);
+    }
+    return {d_input, d_direction};
+  }
+};
+
+at::Tensor frechet_autograd(const at::Tensor& input, const at::Tensor& direction) {
+  return FrechetFunction::apply(input, direction);
+}
+
 struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
   static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& input) {
     static const auto op = c10::Dispatcher::singleton()
@@ -108,15 +167,13 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
 
   static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
                                                  torch::autograd::variable_list grads) {
-    static const auto op = c10::Dispatcher::singleton()
-                               .findSchemaOrThrow("flash_hypercons::_frechet", "")
-                               .typed<at::Tensor(const at::Tensor&, const at::Tensor&)>();
     const at::Tensor input = ctx->get_saved_variables()[0];
     const at::Tensor& grad = grads[0];
-    if (at::GradMode::is_enabled() || has_tangent(input) || has_tangent(grad)) {
-      return {frechet_reference(input.mT(), grad)};
-    }
-    return {op.call(input.mT(), grad)};
+    // Forward-mode tangents need operators with forward derivatives: the native formula.
+    if (has_tangent(input) || has_tangent(grad)) return {frechet_reference(input.mT(), grad)};
+    // With grad mode on (a graph of this backward is being built) the call goes through the
+    // autograd formula of _frechet above; otherwise straight to the kernel.
+    return {frechet_op().call(input.mT(), grad)};
   }
 };
 
@@ -134,7 +191,10 @@ TORCH_LIBRARY_IMPL(flash_hypercons, CUDA, m) {
   m.impl("_frechet", &frechet_cuda);
 }
 
-TORCH_LIBRARY_IMPL(flash_hypercons, Autograd, m) { m.impl("_matrix_exp", &matrix_exp_autograd); }
+TORCH_LIBRARY_IMPL(flash_hypercons, Autograd, m) {
+  m.impl("_matrix_exp", &matrix_exp_autograd);
+  m.impl("_frechet", &frechet_autograd);
+}
 
 static PyModuleDef module_def = {PyModuleDef_HEAD_INIT, "_C", "flash_hypercons operator registration", -1,
                                  nullptr};
