@@ -222,6 +222,38 @@ def time_steps(fh, a, g, steps: int, warmup: int, dist: Dist, flush: torch.Tenso
     return total, statistics.mean(fwd), statistics.mean(bwd)
 
 
+def graph_step_ms(fh, a, g, steps: int, warmup: int, flush: torch.Tensor | None):
+    """Device time per step of one fwd+bwd step captured in a CUDA graph and replayed (the launch-
+    overhead answer for small batches), and whether the replayed results equal an eager step."""
+    x = a.detach().clone().requires_grad_()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            y = fh.matrix_exp(x)
+            torch.autograd.grad(y, x, g)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = fh.matrix_exp(x)
+        (grad,) = torch.autograd.grad(y, x, g)
+    for _ in range(warmup):
+        graph.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        if flush is not None:
+            flush.add_(1.0)
+        e0.record()
+        graph.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    y_eager, grad_eager = fwd_bwd(fh, a, g)
+    same = bool(torch.equal(y, y_eager) and torch.equal(grad, grad_eager))
+    del graph
+    return ms, same
+
+
 # End-to-end pipeline shape (matrices per chunk, streams), measured on B200 over PCIe with
 # config 5: 8192 x 4 gave 5.25 M matrices/s, 32768 x 2 gave 4.45 M, 4096 x 8 gave 5.03 M.
 E2E_CHUNK = 8192
@@ -312,7 +344,7 @@ def load_traffic(config_index: int):
         return None
 
 
-def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, batch=None):
+def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, batch=None, with_graph=False):
     from flash_hyperconnections_b200 import roofline as R
     from flash_hyperconnections_b200 import workloads as W
 
@@ -331,6 +363,7 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
     launches = count_our_launches(fh, a, g)
     total_ms, fwd_ms, bwd_ms = time_steps(fh, a, g, steps, warmup, dist, flush)
     digest = result_digest(fh, a, g)
+    graph = graph_step_ms(fh, a, g, steps, warmup, flush) if with_graph else None
     result = {
         "digest": digest,
         "count": count,
@@ -345,6 +378,8 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         "l2": "L2 flushed (256 MB write) between timed iterations" if flush is not None
         else f"inputs larger than L2 ({in_bytes / 1e9:.2f} GB per tensor per rank)",
     }
+    if graph is not None:
+        result["graph_ms"], result["graph_matches_eager"] = graph
     if with_e2e:
         e2e_count = min(count, 131072)
         a_host = (a[:e2e_count].mT.contiguous() if cfg.transposed else a[:e2e_count]).cpu().pin_memory()
@@ -467,7 +502,8 @@ def main():
             if idx == args.config:
                 continue
             sub = W.CONFIGS[idx]
-            r = measure_config(fh, sub, 0, 1, dist, max(5, args.steps), args.warmup, device, with_e2e=False)
+            r = measure_config(fh, sub, 0, 1, dist, max(5, args.steps), args.warmup, device, with_e2e=False,
+                               with_graph=idx == 2)
             ms = r["total_ms"] / max(5, args.steps)
             extras[sub.name] = {
                 "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
@@ -475,6 +511,12 @@ def main():
                 "fwd_tflops": r["fwd_flops"] / (r["fwd_ms"] * 1e9), "bwd_tflops": r["bwd_flops"] / (r["bwd_ms"] * 1e9),
                 "hbm_gbs": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": r["mean_steps"], "l2": r["l2"],
             }
+            if "graph_ms" in r:
+                extras[sub.name]["cuda_graph"] = {
+                    "ms_per_step": r["graph_ms"], "value": sub.batch / (r["graph_ms"] / 1e3),
+                    "matches_eager": r["graph_matches_eager"],
+                    "path": "one fwd+bwd step (fh.matrix_exp + autograd.grad) captured in torch.cuda.CUDAGraph, replayed",
+                }
         cpu = cpu_reference_sample(cfg, args.cpu_seconds)
 
     if dist.rank == 0:
