@@ -207,10 +207,16 @@ __device__ __forceinline__ float4 load_row4(const View& v, int dtype, int64_t of
   return make_float4(dec(h.x & 0xffffu), dec(h.x >> 16), dec(h.y & 0xffffu), dec(h.y >> 16));
 }
 
+// Threads per CTA of the register kernel.  With at least 8 CTAs per SM the compiler caps the
+// kernel at 128 registers: the 4 x 4 Frechet kernel (204 registers uncapped, 8 warps per SM)
+// then spills only in its degree-18 branch and runs 16 warps per SM.  Measured on B200: config 2
+// backward 12.3 -> 10.3 us, a batch of degree-18 matrices unchanged, results bit-identical.
+constexpr int kRegThreads = 64;
+
 // flags: bit 0 = rows of A are one vector load each, bit 1 = same for E, bit 2 = output rows
 // can be stored as one vector each (N == 4 only).
 template <int N, bool Pair>
-__global__ void __launch_bounds__(128) expm_reg_kernel(View a, View e, void* __restrict__ out, int64_t batch,
+__global__ void __launch_bounds__(kRegThreads, 8) expm_reg_kernel(View a, View e, void* __restrict__ out, int64_t batch,
                                                        int dtype, unsigned flags) {
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= batch) return;

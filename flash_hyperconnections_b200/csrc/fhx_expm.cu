@@ -62,7 +62,7 @@ bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(
 
 template <int N, bool Pair>
 int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype, cudaStream_t stream) {
-  constexpr int threads = 128;
+  constexpr int threads = kRegThreads;
   const int64_t blocks = (batch + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
   // 4 x 4: rows with unit inner stride, 4-element-aligned row and matrix strides and an aligned
