@@ -58,17 +58,19 @@ def timing(lib: str, config: int, batch: int, reps: int, out: str) -> None:
         frechet(a.mT, g)
         expm(a)
     torch.cuda.synchronize()
+    # back-to-back calls between two events: the host enqueues ahead of the GPU, so small batches
+    # measure the operators' device time rather than per-call host latency
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    fwd = bwd = 0.0
+    ev[0].record()
     for _ in range(reps):
-        ev[0].record()
         expm(a)
-        ev[1].record()
+    ev[1].record()
+    for _ in range(reps):
         frechet(a.mT, g)
-        ev[2].record()
-        torch.cuda.synchronize()
-        fwd += ev[0].elapsed_time(ev[1])
-        bwd += ev[1].elapsed_time(ev[2])
+    ev[2].record()
+    torch.cuda.synchronize()
+    fwd = ev[0].elapsed_time(ev[1])
+    bwd = ev[1].elapsed_time(ev[2])
     pathlib.Path(out).write_text(json.dumps({"count": a.shape[0], "fwd_ms": fwd / reps, "bwd_ms": bwd / reps}))
 
 
