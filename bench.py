@@ -322,6 +322,14 @@ def e2e_steps(fh, cfg, a_host, g_host, steps: int, warmup: int, dist: Dist, devi
 # ----------------------------------------------------------------------------------------
 # roofline
 # ----------------------------------------------------------------------------------------
+def frechet_kernel_name(n: int) -> str:
+    """The kernel that fhx_frechet launches for n x n matrices (the roofline's dominant kernel)."""
+    if n <= 4:
+        return f"fhx::expm_reg_kernel<{n}, Frechet> (fhx_frechet)"
+    tile = {8: "8, 4, 4", 16: "16, 2, 4", 32: "32, 2, 4"}[8 if n <= 8 else 16 if n <= 16 else 32]
+    return f"fhx::expm_team_kernel<{tile}, Frechet> (fhx_frechet)"
+
+
 def load_peaks():
     try:
         with open(PEAKS_PATH) as f:
@@ -529,7 +537,7 @@ def main():
         traffic = load_traffic(args.config)
         roofline = {
             "bound": "fp32_fma",
-            "kernel": "fhx::expm_team_kernel<32, Frechet> (fhx_frechet)",
+            "kernel": frechet_kernel_name(cfg.n),
             "achieved": bwd_tflops,
             "peak": fma_peak,
             "unit": "TFLOP/s",
