@@ -319,6 +319,38 @@ def e2e_steps(fh, cfg, a_host, g_host, steps: int, warmup: int, dist: Dist, devi
     return elapsed, 2 * nbytes, 2 * nbytes
 
 
+def link_gbs_per_direction(device, nbytes: int = 256 << 20) -> float:
+    """Pinned host<->device copy bandwidth of this rank's link with both directions running at once
+    (the bound of the e2e leg, which uploads and downloads concurrently), GB/s per direction."""
+    h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    d_out = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    up, down = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+
+    def both():
+        cur = torch.cuda.current_stream(device)
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        with torch.cuda.stream(up):
+            d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(down):
+            h_out.copy_(d_out, non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+
+    both()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    start.record()
+    for _ in range(reps):
+        both()
+    end.record()
+    torch.cuda.synchronize(device)
+    return reps * nbytes / (start.elapsed_time(end) * 1e6)
+
+
 # ----------------------------------------------------------------------------------------
 # roofline
 # ----------------------------------------------------------------------------------------
@@ -395,7 +427,8 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         del a, g
         torch.cuda.empty_cache()
         sec, h2d, d2h = e2e_steps(fh, cfg, a_host, g_host, max(2, min(steps, 5)), 1, dist, device)
-        result["e2e"] = {"sec_per_step": sec, "count": e2e_count, "h2d": h2d, "d2h": d2h}
+        result["e2e"] = {"sec_per_step": sec, "count": e2e_count, "h2d": h2d, "d2h": d2h,
+                         "link_gbs": link_gbs_per_direction(device)}
     return result
 
 
@@ -502,6 +535,12 @@ def main():
                "d2h_bytes_per_step": main_res["e2e"]["d2h"] * dist.world,
                "batch": e2e_total, "path": "pinned host -> fh.matrix_exp + autograd.grad -> pinned host, "
                                            f"{E2E_STREAMS} streams, {E2E_CHUNK}-matrix chunks"}
+        # the e2e leg's own roofline: each rank's host link, both directions at once
+        link = -dist.max(-main_res["e2e"]["link_gbs"])  # slowest rank's link
+        per_dir = main_res["e2e"]["h2d"] / (sec * 1e9)    # bytes each way per rank per second
+        e2e["link"] = {"bound": "pcie", "achieved_gbs_per_direction": per_dir,
+                       "measured_gbs_per_direction": link, "frac": per_dir / link,
+                       "measured": "pinned 256 MB host->device and device->host copies on two streams at once"}
 
     extras = {}
     cpu = None
