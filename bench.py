@@ -30,6 +30,7 @@ sys.path.insert(0, ROOT)
 
 HEADLINE = 5
 METRIC = "fwd+bwd matrices/s"
+SECONDARY = (2, 4)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "ncu_traffic.json")
 
@@ -46,6 +47,22 @@ def parse_args():
     p.add_argument("--batch", type=int, default=None,
                    help="use only the first BATCH matrices of the config (small cases for profiling)")
     return p.parse_args()
+
+
+def workloads_module():
+    """``flash_hyperconnections_b200/workloads.py`` loaded by file path.  It needs torch only;
+    importing it through the package would run the package ``__init__``, which loads this
+    repository's native libraries -- and the reference arm must not map them."""
+    import importlib.util
+
+    name = "_fhx_bench_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "flash_hyperconnections_b200", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod  # dataclasses resolve their module through sys.modules
+    spec.loader.exec_module(mod)
+    return mod
 
 
 # ----------------------------------------------------------------------------------------
@@ -86,6 +103,14 @@ class Dist:
         device = f"cuda:{self.local_rank}" if self.backend == "nccl" else "cpu"
         t = torch.tensor([value], dtype=torch.float64, device=device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        device = f"cuda:{self.local_rank}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
 
     def sum_ints(self, values: list[int]) -> list[int]:
@@ -319,9 +344,15 @@ def e2e_steps(fh, cfg, a_host, g_host, steps: int, warmup: int, dist: Dist, devi
     return elapsed, 2 * nbytes, 2 * nbytes
 
 
-def link_gbs_per_direction(device, nbytes: int = 256 << 20) -> float:
+LINK_BYTES = 256 << 20
+LINK_REPS = 8
+
+
+def link_gbs_per_direction(device, dist: Dist, nbytes: int = LINK_BYTES, reps: int = LINK_REPS) -> float:
     """Pinned host<->device copy bandwidth of this rank's link with both directions running at once
-    (the bound of the e2e leg, which uploads and downloads concurrently), GB/s per direction."""
+    (the bound of the e2e leg, which uploads and downloads concurrently), GB/s per direction.  The
+    ranks start together (barrier) so that the figure includes the host-memory and PCIe-switch
+    sharing that the e2e leg itself sees at N > 1."""
     h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     d_in = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -341,13 +372,15 @@ def link_gbs_per_direction(device, nbytes: int = 256 << 20) -> float:
 
     both()
     torch.cuda.synchronize(device)
+    dist.barrier()
+    torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
     start.record()
     for _ in range(reps):
         both()
     end.record()
     torch.cuda.synchronize(device)
+    dist.barrier()
     return reps * nbytes / (start.elapsed_time(end) * 1e6)
 
 
@@ -386,7 +419,8 @@ def load_traffic(config_index: int):
 
 def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, batch=None, with_graph=False):
     from flash_hyperconnections_b200 import roofline as R
-    from flash_hyperconnections_b200 import workloads as W
+
+    W = workloads_module()
 
     start, count = W.shard(cfg, rank, world) if world > 1 else (0, cfg.batch)
     if batch is not None:
@@ -428,7 +462,7 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         torch.cuda.empty_cache()
         sec, h2d, d2h = e2e_steps(fh, cfg, a_host, g_host, max(2, min(steps, 5)), 1, dist, device)
         result["e2e"] = {"sec_per_step": sec, "count": e2e_count, "h2d": h2d, "d2h": d2h,
-                         "link_gbs": link_gbs_per_direction(device)}
+                         "link_gbs": link_gbs_per_direction(device, dist)}
     return result
 
 
@@ -436,8 +470,9 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
 # CPU path of the reference (native torch + autograd on the host cores)
 # ----------------------------------------------------------------------------------------
 def cpu_reference_sample(cfg, target_seconds: float):
-    from flash_hyperconnections_b200 import workloads as W
     from oracle import cpu_path
+
+    W = workloads_module()
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -457,8 +492,9 @@ def cpu_reference_sample(cfg, target_seconds: float):
 
 
 def run_reference(args, dist):
-    from flash_hyperconnections_b200 import workloads as W
     from oracle import cpu_path
+
+    W = workloads_module()
 
     cfg = W.CONFIGS[args.config]
     if dist.rank != 0:
@@ -505,8 +541,8 @@ def main():
         return
 
     import flash_hypercons as fh
-    from flash_hyperconnections_b200 import workloads as W
 
+    W = workloads_module()
     device = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(device)
     dist.init("nccl")
@@ -523,6 +559,10 @@ def main():
     total_ms = dist.max(main_res["total_ms"])
     fwd_ms = dist.max(main_res["fwd_ms"])
     bwd_ms = dist.max(main_res["bwd_ms"])
+    # algorithmic work of the whole job (every rank's shard), for the per-GPU roofline
+    fwd_flops = dist.sum(main_res["fwd_flops"])
+    bwd_flops = dist.sum(main_res["bwd_flops"])
+    sum_steps = dist.sum(main_res["mean_steps"] * main_res["count"])
     ms_per_step = total_ms / args.steps
     global_batch = main_res["count"] * dist.world
     value = global_batch / (ms_per_step / 1e3)
@@ -535,28 +575,43 @@ def main():
                "d2h_bytes_per_step": main_res["e2e"]["d2h"] * dist.world,
                "batch": e2e_total, "path": "pinned host -> fh.matrix_exp + autograd.grad -> pinned host, "
                                            f"{E2E_STREAMS} streams, {E2E_CHUNK}-matrix chunks"}
-        # the e2e leg's own roofline: each rank's host link, both directions at once
+        # the e2e leg's own roofline: each rank's host link, both directions at once, measured
+        # with every rank copying at the same time
         link = -dist.max(-main_res["e2e"]["link_gbs"])  # slowest rank's link
         per_dir = main_res["e2e"]["h2d"] / (sec * 1e9)    # bytes each way per rank per second
         e2e["link"] = {"bound": "pcie", "achieved_gbs_per_direction": per_dir,
                        "measured_gbs_per_direction": link, "frac": per_dir / link,
-                       "measured": "pinned 256 MB host->device and device->host copies on two streams at once"}
+                       "aggregate_host_gbs": 2 * per_dir * dist.world,
+                       "measured": f"pinned {LINK_BYTES >> 20} MB host->device and device->host copies on two streams "
+                                   f"at once, x{LINK_REPS}, all ranks together"}
 
     extras = {}
-    cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_extras:
-        for idx in (2, 4):
+    if not args.no_extras:
+        # Secondary configs, sharded over the ranks like the headline one (same collective steps
+        # on every rank).
+        for idx in SECONDARY:
             if idx == args.config:
                 continue
             sub = W.CONFIGS[idx]
-            r = measure_config(fh, sub, 0, 1, dist, max(5, args.steps), args.warmup, device, with_e2e=False,
-                               with_graph=idx == 2)
-            ms = r["total_ms"] / max(5, args.steps)
+            steps = max(5, args.steps)
+            r = measure_config(fh, sub, dist.rank, dist.world, dist, steps, args.warmup, device, with_e2e=False,
+                               with_graph=idx == 2 and dist.world == 1)
+            sub_digest = dist.sum_ints(r["digest"])
+            sub_total = dist.max(r["total_ms"])
+            sub_fwd = dist.max(r["fwd_ms"])
+            sub_bwd = dist.max(r["bwd_ms"])
+            sub_fwd_flops = dist.sum(r["fwd_flops"]) / dist.world
+            sub_bwd_flops = dist.sum(r["bwd_flops"]) / dist.world
+            sub_steps = dist.sum(r["mean_steps"] * r["count"])
+            ms = sub_total / steps
             extras[sub.name] = {
-                "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
-                "fwd_kernel_ms": r["fwd_ms"], "bwd_kernel_ms": r["bwd_ms"],
-                "fwd_tflops": r["fwd_flops"] / (r["fwd_ms"] * 1e9), "bwd_tflops": r["bwd_flops"] / (r["bwd_ms"] * 1e9),
-                "hbm_gbs": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": r["mean_steps"], "l2": r["l2"],
+                "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms, "n_gpus": dist.world,
+                "result_digest": {"y_bits_sum": sub_digest[0], "grad_bits_sum": sub_digest[1]},
+                "fwd_kernel_ms": sub_fwd, "bwd_kernel_ms": sub_bwd,
+                "fwd_tflops_per_gpu": sub_fwd_flops / (sub_fwd * 1e9),
+                "bwd_tflops_per_gpu": sub_bwd_flops / (sub_bwd * 1e9),
+                "hbm_gbs_per_gpu": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": sub_steps / sub.batch,
+                "l2": r["l2"],
             }
             if "graph_ms" in r:
                 extras[sub.name]["cuda_graph"] = {
@@ -564,6 +619,8 @@ def main():
                     "matches_eager": r["graph_matches_eager"],
                     "path": "one fwd+bwd step (fh.matrix_exp + autograd.grad) captured in torch.cuda.CUDAGraph, replayed",
                 }
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_extras:
         cpu = cpu_reference_sample(cfg, args.cpu_seconds)
 
     if dist.rank == 0:
@@ -571,9 +628,11 @@ def main():
         props = torch.cuda.get_device_properties(device)
         max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
         fma_peak = fp32_fma_peak_tflops(props.multi_processor_count, max_mhz)
-        bwd_tflops = main_res["bwd_flops"] / (bwd_ms * 1e9)  # rank-0 shard flops over the max-rank time
-        fwd_tflops = main_res["fwd_flops"] / (fwd_ms * 1e9)
+        # per GPU: the job's algorithmic flops / N over the max-over-ranks kernel time
+        bwd_tflops = bwd_flops / dist.world / (bwd_ms * 1e9)
+        fwd_tflops = fwd_flops / dist.world / (fwd_ms * 1e9)
         traffic = load_traffic(args.config)
+        hbm_gbs = main_res["bytes"] / (ms_per_step * 1e6)
         roofline = {
             "bound": "fp32_fma",
             "kernel": frechet_kernel_name(cfg.n),
@@ -585,9 +644,12 @@ def main():
                            f"{max_mhz:.0f} MHz (clocks.max.sm, {peak_src} MEASURED_PEAKS.json has no FP32-FMA figure)",
             "traffic": traffic,
             "forward": {"achieved": fwd_tflops, "frac": fwd_tflops / fma_peak},
-            "hbm": {"achieved_gbs": main_res["bytes"] / (ms_per_step * 1e6), "peak_gbs": peaks.get("hbm_gbs"),
-                    "frac": main_res["bytes"] / (ms_per_step * 1e6) / float(peaks.get("hbm_gbs", 6650.0))},
-            "flops_definition": "2 P^3 (pi(m)+s) fwd, 6 P^3 (pi(m)+s) bwd per matrix, (m, s) from the kernel's rule",
+            "step": {"achieved": (fwd_flops + bwd_flops) / dist.world / (ms_per_step * 1e9),
+                     "frac": (fwd_flops + bwd_flops) / dist.world / (ms_per_step * 1e9) / fma_peak},
+            "hbm": {"achieved_gbs_per_gpu": hbm_gbs, "peak_gbs": peaks.get("hbm_gbs"),
+                    "frac": hbm_gbs / float(peaks.get("hbm_gbs", 6650.0))},
+            "flops_definition": "2 P^3 (pi(m)+s) fwd, 6 P^3 (pi(m)+s) bwd per matrix, (m, s) from the kernel's rule; "
+                                "summed over every rank's shard, per GPU",
         }
         if clocks and clocks.get("sm_mhz"):
             roofline["frac_at_sampled_clock"] = bwd_tflops / fp32_fma_peak_tflops(props.multi_processor_count,
@@ -597,6 +659,8 @@ def main():
             "value": value,
             "unit": "matrices/s",
             "n_gpus": dist.world,
+            "result_digest": {"y_bits_sum": digest[0], "grad_bits_sum": digest[1],
+                              "note": "sum over ranks of the raw bits of Y and the gradient; the same at every GPU count"},
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": ms_per_step,
@@ -604,14 +668,13 @@ def main():
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "f32",
-            "data": "synthetic (seeded config generator; see flash_hyperconnections_b200/workloads.py)",
+            "data": "synthetic (seeded host-side generator, same matrices at every GPU count and in the CPU arm; "
+                    "see flash_hyperconnections_b200/workloads.py)",
             "config": {"workload": f"config{cfg.index}:{cfg.name} fwd+bwd", "global_batch": global_batch, "n": cfg.n,
                        "io_dtype": str(cfg.dtype).replace("torch.", ""), "parallelism": f"batch shards x{dist.world}, "
                        "no collective", "l2": main_res["l2"],
-                       "mean_products_per_matrix": main_res["mean_steps"]},
+                       "mean_products_per_matrix": sum_steps / global_batch},
             "gpu_launches": main_res["launches_per_step"] * args.steps,
-            "result_digest": {"y_bits_sum": digest[0], "grad_bits_sum": digest[1],
-                              "note": "sum over ranks of the raw bits of Y and the gradient; the same at every GPU count"},
             "kernel_ms": {"fwd": fwd_ms / 1.0, "bwd": bwd_ms / 1.0},
             "roofline": roofline,
             "clocks": clocks,

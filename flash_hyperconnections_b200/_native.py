@@ -41,4 +41,8 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_status_string.restype = ctypes.c_char_p
     lib.fhx_abi_version.argtypes = []
     lib.fhx_abi_version.restype = i32
+    lib.fhx_last_cuda_error.argtypes = []
+    lib.fhx_last_cuda_error.restype = i32
+    lib.fhx_last_cuda_error_string.argtypes = []
+    lib.fhx_last_cuda_error_string.restype = ctypes.c_char_p
     return lib

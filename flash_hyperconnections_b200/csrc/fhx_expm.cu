@@ -27,6 +27,16 @@ struct DeviceInfo {
 std::mutex g_mutex;
 DeviceInfo g_devices[kMaxDevices];
 
+// The CUDA error behind the calling thread's last FHX_ERR_CUDA.
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+// Status of a CUDA runtime result; a failure is remembered for fhx_last_cuda_error().
+int cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return FHX_OK;
+  g_last_cuda_error = err;
+  return FHX_ERR_CUDA;
+}
+
 // Per-(kernel, device) launch geometry: resident CTAs per SM at the kernel's smem size.
 struct LaunchShape {
   bool ready[kMaxDevices] = {};
@@ -37,7 +47,7 @@ int device_sms(int dev) {
   std::lock_guard<std::mutex> lock(g_mutex);
   DeviceInfo& d = g_devices[dev];
   if (!d.ready) {
-    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (cuda_status(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != FHX_OK) return -1;
     d.ready = true;
   }
   return d.sms;
@@ -48,10 +58,11 @@ int resident_blocks(Kernel kernel, LaunchShape& shape, int dev, int threads, siz
   std::lock_guard<std::mutex> lock(g_mutex);
   if (!shape.ready[dev]) {
     if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))) != FHX_OK)
       return -1;
     int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem) != cudaSuccess) return -1;
+    if (cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem)) != FHX_OK)
+      return -1;
     shape.blocks_per_sm[dev] = blocks > 0 ? blocks : 1;
     shape.ready[dev] = true;
   }
@@ -76,7 +87,7 @@ int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype
   if (Pair && rows(e)) flags |= 2u;
   if (N == 4 && aligned(out, row_bytes)) flags |= 4u;
   expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, batch, dtype, flags);
-  return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
+  return cuda_status(cudaGetLastError());
 }
 
 // Load/store layout flags of the team kernel (see the enum in expm_team.cuh).
@@ -103,8 +114,8 @@ unsigned layout_flags(const View& a, const View& e, const void* out, int n, int 
   return f;
 }
 
-// TN: columns of a thread's register tile; WARPS: warps per CTA.  A team is
-// (P/4) * (P/TN) threads; one CTA holds WARPS * 32 / team-size teams.
+// TM x TN: a thread's register tile; WARPS: warps per CTA.  A team is (P/TM) * (P/TN)
+// threads; one CTA holds WARPS * 32 / team-size teams.
 template <int P, int TM, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
   using C = TeamCfg<P, TM, TN, Pair>;
@@ -114,7 +125,9 @@ int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, i
   static LaunchShape shape;
   auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS>;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
+  const int st = cuda_status(cudaGetDevice(&dev));
+  if (st != FHX_OK) return st;
+  if (dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
   const int sms = device_sms(dev);
   const int per_sm = resident_blocks(kernel, shape, dev, threads, smem);
   if (sms <= 0 || per_sm <= 0) return FHX_ERR_CUDA;
@@ -122,7 +135,7 @@ int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, i
   const int64_t resident = int64_t(sms) * per_sm;
   const int blocks = int(items < resident ? items : resident);
   kernel<<<blocks, threads, smem, stream>>>(a, e, out, batch, n, dtype, layout_flags<P>(a, e, out, n, dtype, Pair));
-  return cudaGetLastError() == cudaSuccess ? FHX_OK : FHX_ERR_CUDA;
+  return cuda_status(cudaGetLastError());
 }
 
 template <bool Pair>
@@ -209,11 +222,15 @@ const char* fhx_status_string(int32_t status) {
     case FHX_ERR_DTYPE: return "dtype must be float32, bfloat16 or float16";
     case FHX_ERR_POINTER: return "null data pointer for a non-empty batch";
     case FHX_ERR_STRIDE: return "negative stride";
-    case FHX_ERR_CUDA: return "CUDA launch failed";
+    case FHX_ERR_CUDA: return "a CUDA runtime call or kernel launch failed (see fhx_last_cuda_error)";
     default: return "unknown status";
   }
 }
 
-int32_t fhx_abi_version(void) { return 100; }
+int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda_error); }
+
+const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
+
+int32_t fhx_abi_version(void) { return 101; }
 
 }  // extern "C"

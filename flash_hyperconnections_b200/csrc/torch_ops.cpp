@@ -28,6 +28,7 @@
 #include <ATen/ops/zeros_like.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/csrc/autograd/custom_function.h>
+#include <torch/csrc/autograd/forward_grad.h>
 #include <torch/library.h>
 
 #include "fhx.h"
@@ -73,7 +74,8 @@ at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
                          e.const_data_ptr(), e.stride(0), e.stride(1), e.stride(2), e.is_neg() ? 1 : 0,
                          out.mutable_data_ptr(), batch, n, dtype_code(a), stream);
   }
-  TORCH_CHECK(status == FHX_OK, "flash_hypercons kernel: ", fhx_status_string(status));
+  TORCH_CHECK(status == FHX_OK, "flash_hypercons kernel: ", fhx_status_string(status),
+              status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
   return out;
 }
 
@@ -92,7 +94,21 @@ at::Tensor frechet_reference(const at::Tensor& input, const at::Tensor& directio
   return at::linalg_matrix_exp(at::cat({top, bottom}, -2)).slice(-2, 0, n).slice(-1, n, 2 * n).to(input.scalar_type());
 }
 
-bool has_tangent(const at::Tensor& t) { return t.defined() && t._fw_grad(/*level=*/0).defined(); }
+// A forward-mode tangent at any live forward-AD level (levels nest, so the live ones are
+// 0, 1, ... up to the first released index).
+bool has_tangent(const at::Tensor& t) {
+  if (!t.defined()) return false;
+  for (uint64_t level = 0; level < 64; ++level) {
+    if (!torch::autograd::ForwardADLevel::try_get_by_idx(level)) break;
+    if (t._fw_grad(level).defined()) return true;
+  }
+  return false;
+}
+
+// A tensor subclass with Python dispatch (__torch_dispatch__): it must see the native
+// operators of the block formula, not this package's operator (the reference's
+// has_torch_function check, flash_hypercons/ops/matrix_exp/__init__.py:66-72).
+bool is_python_tensor(const at::Tensor& t) { return t.defined() && t.key_set().has(c10::DispatchKey::Python); }
 
 const auto& frechet_op() {
   static const auto op = c10::Dispatcher::singleton()
@@ -169,8 +185,10 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
                                                  torch::autograd::variable_list grads) {
     const at::Tensor input = ctx->get_saved_variables()[0];
     const at::Tensor& grad = grads[0];
-    // Forward-mode tangents need operators with forward derivatives: the native formula.
-    if (has_tangent(input) || has_tangent(grad)) return {frechet_reference(input.mT(), grad)};
+    // Forward-mode tangents need operators with forward derivatives, and tensor subclasses
+    // must see native operators: the native formula.
+    if (has_tangent(input) || has_tangent(grad) || is_python_tensor(input) || is_python_tensor(grad))
+      return {frechet_reference(input.mT(), grad)};
     // With grad mode on (a graph of this backward is being built) the call goes through the
     // autograd formula of _frechet above; otherwise straight to the kernel.
     return {frechet_op().call(input.mT(), grad)};

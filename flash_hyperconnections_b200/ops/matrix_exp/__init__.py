@@ -1,3 +1,7 @@
+# Interface (function names, predicates, fakes, public docstrings) follows
+# nickjeliopoulos/flash-hyperconnections, flash_hypercons/ops/matrix_exp/__init__.py.
+# Copyright (c) 2023-2026 Nicholas John Eliopoulos, Purvish Jatin Jajal.  MIT License; the full
+# permission notice is in tests/LICENSE.flash-hyperconnections.
 """Python operator layer: eligibility, native routing, fake kernels, scoped routing.
 
 Behaviour mirrors flash_hypercons/ops/matrix_exp/__init__.py of the reference package

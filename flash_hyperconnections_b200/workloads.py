@@ -1,9 +1,10 @@
 """Seeded synthetic inputs of the five benchmark configurations.
 
 Every config is generated in fixed chunks of ``CHUNK`` matrices, chunk c drawing from its own
-generator seeded with ``seed * 1_000_003 + c``.  Any contiguous shard that starts on a chunk
-boundary (every 1/2/4/8-way split of the configs does) is therefore bit-identical whichever
-rank or process generates it, so 1-GPU and 8-GPU runs see the same matrices.
+host (CPU) generator seeded with ``seed * 1_000_003 + c``, and then copied to the target
+device.  Any contiguous shard that starts on a chunk boundary (every 1/2/4/8-way split of the
+configs does) is therefore bit-identical whichever rank, process or device generates it: 1-GPU
+and 8-GPU runs, and the CPU baseline, see the same matrices.
 
 1. FP32 [128, 4, 4], entries N(0, 1); upstream gradient all ones.
 2. BF16 [65536, 4, 4], entries N(0, 0.1^2) (hyper-connection stream mixing); gradient N(0, 1).
@@ -16,6 +17,8 @@ rank or process generates it, so 1-GPU and 8-GPU runs see the same matrices.
 
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import torch
@@ -50,57 +53,67 @@ CONFIGS = {
 }
 
 
-def _chunk(cfg: Config, c: int, count: int, device) -> tuple[torch.Tensor, torch.Tensor]:
-    g = torch.Generator(device=device)
+def _chunk(cfg: Config, c: int, count: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Chunk ``c`` of ``cfg``: ``count`` matrices and gradients, drawn on the host."""
+    g = torch.Generator(device="cpu")
     g.manual_seed(cfg.seed * 1_000_003 + c)
     n = cfg.n
     shape = (count, n, n)
     if cfg.index == 1:
-        a = torch.randn(shape, generator=g, device=device)
-        grad = torch.ones(shape, device=device)
+        a = torch.randn(shape, generator=g)
+        grad = torch.ones(shape)
     elif cfg.index == 2:
-        a = torch.randn(shape, generator=g, device=device) * 0.1
-        grad = torch.randn(shape, generator=g, device=device)
+        a = torch.randn(shape, generator=g) * 0.1
+        grad = torch.randn(shape, generator=g)
     elif cfg.index == 3:
-        a = torch.randn(shape, generator=g, device=device) / n**0.5
-        u = torch.rand((count, 1, 1), generator=g, device=device) * 4 - 3
+        a = torch.randn(shape, generator=g) / n**0.5
+        u = torch.rand((count, 1, 1), generator=g) * 4 - 3
         a = a * torch.pow(10.0, u)
-        grad = torch.randn(shape, generator=g, device=device)
+        grad = torch.randn(shape, generator=g)
     elif cfg.index == 4:
-        m = torch.randn(shape, generator=g, device=device) * 0.25
+        m = torch.randn(shape, generator=g) * 0.25
         a = (m - m.mT) / 2
-        grad = torch.randn(shape, generator=g, device=device)
+        grad = torch.randn(shape, generator=g)
     elif cfg.index == 5:
-        a = torch.randn(shape, generator=g, device=device) / n**0.5
-        scale = torch.exp(torch.randn((count, 1, 1), generator=g, device=device))
+        a = torch.randn(shape, generator=g) / n**0.5
+        scale = torch.exp(torch.randn((count, 1, 1), generator=g))
         a = a * scale
-        grad = torch.randn(shape, generator=g, device=device)
+        grad = torch.randn(shape, generator=g)
     else:
         raise ValueError(cfg.index)
     return a.to(cfg.dtype), grad.to(cfg.dtype)
 
 
-def generate(cfg: Config, start: int = 0, count: int | None = None, device="cpu"):
-    """Matrices [start, start + count) of ``cfg`` and their upstream gradients.
+def generate(cfg: Config, start: int = 0, count: int | None = None, device="cpu", workers: int | None = None):
+    """Matrices [start, start + count) of ``cfg`` and their upstream gradients, on ``device``.
 
-    ``start`` must be a multiple of CHUNK (or 0).  For config 3 the returned input is the
-    transposed view of a contiguous buffer, as the config prescribes.
+    ``start`` must be a multiple of CHUNK (or 0).  Chunks are drawn on the host in parallel
+    (``workers`` threads, each chunk with its own generator, so the result does not depend on
+    the thread count) and copied into the output tensors.  For config 3 the returned input is
+    the transposed view of a contiguous buffer, as the config prescribes.
     """
     count = cfg.batch - start if count is None else count
     if start % CHUNK:
         raise ValueError("start must be a multiple of CHUNK")
-    parts_a, parts_g = [], []
-    c = start // CHUNK
-    remaining = count
-    while remaining > 0:
-        take = min(CHUNK, remaining)
-        a, g = _chunk(cfg, c, CHUNK if cfg.batch >= CHUNK else cfg.batch, device)
-        parts_a.append(a[:take])
-        parts_g.append(g[:take])
-        remaining -= take
-        c += 1
-    a = torch.cat(parts_a) if len(parts_a) > 1 else parts_a[0]
-    g = torch.cat(parts_g) if len(parts_g) > 1 else parts_g[0]
+    n = cfg.n
+    a = torch.empty((count, n, n), dtype=cfg.dtype, device=device)
+    g = torch.empty((count, n, n), dtype=cfg.dtype, device=device)
+    jobs = [(start // CHUNK + i, lo, min(CHUNK, count - lo)) for i, lo in enumerate(range(0, count, CHUNK))]
+
+    def fill(job):
+        c, lo, take = job
+        ca, cg = _chunk(cfg, c, CHUNK if cfg.batch >= CHUNK else cfg.batch)
+        a[lo : lo + take].copy_(ca[:take])
+        g[lo : lo + take].copy_(cg[:take])
+
+    if workers is None:
+        workers = min(16, os.cpu_count() or 1)
+    if workers <= 1 or len(jobs) <= 1:
+        for job in jobs:
+            fill(job)
+    else:
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            list(pool.map(fill, jobs))
     if cfg.transposed:
         a = a.mT.contiguous().mT  # the stored buffer holds A^T; the view reads as A
     return a, g

@@ -38,7 +38,8 @@ extern "C" {
 #define FHX_ERR_DTYPE 2      /* dtype not one of FHX_DTYPE_*                            */
 #define FHX_ERR_POINTER 3    /* null data pointer with batch > 0                        */
 #define FHX_ERR_STRIDE 4     /* negative stride                                         */
-#define FHX_ERR_CUDA 5       /* a CUDA runtime call or the kernel launch failed         */
+#define FHX_ERR_CUDA 5       /* a CUDA runtime call or the kernel launch failed; the
+                                cudaError_t is kept for fhx_last_cuda_error()            */
 
 #define FHX_MAX_N 32
 
@@ -69,6 +70,16 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
 
 /* Static description of a status code. */
 const char* fhx_status_string(int32_t status);
+
+/*
+ * The cudaError_t behind the calling thread's most recent FHX_ERR_CUDA (cudaSuccess = 0 if
+ * none), and its cudaGetErrorString text.  The launch check reads cudaGetLastError(), so an
+ * earlier asynchronous fault still pending on the device is reported by the next call, as
+ * with any CUDA launch check.  (The reference's C10_CUDA_KERNEL_LAUNCH_CHECK,
+ * csrc/matrix_exp.cu:32, reports the same cudaGetErrorString text in its exception.)
+ */
+int32_t fhx_last_cuda_error(void);
+const char* fhx_last_cuda_error_string(void);
 
 /* ABI version of this library (major * 100 + minor). */
 int32_t fhx_abi_version(void);

@@ -1,3 +1,6 @@
+# Test cases adapted from nickjeliopoulos/flash-hyperconnections (tests/reference.py).
+# Copyright (c) 2023-2026 Nicholas John Eliopoulos, Purvish Jatin Jajal.  MIT License; the full
+# permission notice is in tests/LICENSE.flash-hyperconnections.
 """Test helpers mirroring the reference's tests/reference.py (float64 ground truth and the
 per-matrix error criterion), backed by the CPU oracle in oracle/expm_oracle.py."""
 

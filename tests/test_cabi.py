@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_cabi()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.fhx_abi_version() == 100
+    assert lib.fhx_abi_version() == 101
 
 
 def test_status_strings():
@@ -39,6 +39,9 @@ def test_status_strings():
     for code in range(0, 6):
         assert lib.fhx_status_string(code)
     assert b"unknown" in lib.fhx_status_string(99)
+    # no CUDA call has failed on this thread: the remembered error is cudaSuccess
+    assert lib.fhx_last_cuda_error() == 0
+    assert lib.fhx_last_cuda_error_string()
 
 
 @pytest.mark.parametrize(

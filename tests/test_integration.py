@@ -1,3 +1,6 @@
+# Test cases adapted from nickjeliopoulos/flash-hyperconnections (tests/test_integration.py).
+# Copyright (c) 2023-2026 Nicholas John Eliopoulos, Purvish Jatin Jajal.  MIT License; the full
+# permission notice is in tests/LICENSE.flash-hyperconnections.
 """PyTorch integration, case for case the reference's tests/test_integration.py: opcheck,
 higher derivatives, forward AD, torch.func transforms, torch.compile capture, autocast and
 parameters."""

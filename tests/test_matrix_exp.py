@@ -1,3 +1,6 @@
+# Test cases adapted from nickjeliopoulos/flash-hyperconnections (tests/test_matrix_exp.py).
+# Copyright (c) 2023-2026 Nicholas John Eliopoulos, Purvish Jatin Jajal.  MIT License; the full
+# permission notice is in tests/LICENSE.flash-hyperconnections.
 """Numerical behaviour of the CUDA path, case for case the reference's
 tests/test_matrix_exp.py (sizes, dtypes, views, launch and scaling boundaries, non-finite
 inputs, rotations, streams, devices), checked against the float64 oracle."""

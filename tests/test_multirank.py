@@ -81,3 +81,26 @@ def test_reference_arm_under_torchrun():
     assert line["impl"] == "reference" and line["value"] > 0 and line["n_gpus"] == 2
     assert line["cpu_baseline"]["kind"] == "reference"
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+_MAPS_PROBE = """
+import json, runpy, sys
+sys.argv = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0", "--cpu-seconds", "0.5", "--config", "1"]
+runpy.run_path(sys.argv_path, run_name="__main__")
+maps = open("/proc/self/maps").read()
+mapped = sorted({line.split()[-1] for line in maps.splitlines() if "flash_hyperconnections_b200" in line})
+print(json.dumps({"mapped": mapped, "package_imported": "flash_hyperconnections_b200" in sys.modules}))
+"""
+
+
+def test_reference_arm_maps_no_native_library_of_this_package():
+    """The reference arm times the reference's own CPU path: its process must not load this
+    package's native libraries (``_C.so``, ``libfhx.so``), nor import the package at all."""
+    code = _MAPS_PROBE.replace("sys.argv_path", repr(os.path.join(ROOT, "bench.py")))
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [json.loads(line) for line in res.stdout.splitlines() if line.startswith("{")]
+    bench_line, probe = lines[0], lines[-1]
+    assert bench_line["impl"] == "reference"
+    assert probe["mapped"] == [], probe
+    assert probe["package_imported"] is False

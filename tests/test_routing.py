@@ -1,3 +1,6 @@
+# Test cases adapted from nickjeliopoulos/flash-hyperconnections (tests/test_routing.py).
+# Copyright (c) 2023-2026 Nicholas John Eliopoulos, Purvish Jatin Jajal.  MIT License; the full
+# permission notice is in tests/LICENSE.flash-hyperconnections.
 """Scoped routing of torch.linalg.matrix_exp / torch.matrix_exp / Tensor.matrix_exp, case for
 case the reference's tests/test_routing.py.  The CPU cases run without a GPU."""
 
@@ -121,3 +124,15 @@ def test_tensor_subclass_fallback():
     assert isinstance(y, SubTensor)
     assert "flash_hypercons::_matrix_exp" not in names
     torch.testing.assert_close(y, torch.linalg.matrix_exp(a))
+
+
+def test_reference_module_paths_import():
+    # Code written against the original package imports its submodules by path.
+    import importlib
+
+    mod = importlib.import_module("flash_hypercons.ops.matrix_exp")
+    from flash_hypercons.ops.matrix_exp import _eligible, _MatrixExpMode, _native, matrix_exp, use_backend  # noqa: F401
+
+    assert mod.matrix_exp is fh.matrix_exp
+    assert importlib.import_module("flash_hypercons._C") is fh._C
+    assert not _eligible(torch.zeros(2, 4, 4))
