@@ -37,6 +37,8 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_matrix_exp.restype = i32
     lib.fhx_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i64, i32, i32, vp]
     lib.fhx_frechet.restype = i32
+    lib.fhx_matrix_exp_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i32, vp, i64, i32, i32, vp]
+    lib.fhx_matrix_exp_frechet.restype = i32
     lib.fhx_status_string.argtypes = [i32]
     lib.fhx_status_string.restype = ctypes.c_char_p
     lib.fhx_abi_version.argtypes = []

@@ -214,10 +214,13 @@ __device__ __forceinline__ float4 load_row4(const View& v, int dtype, int64_t of
 constexpr int kRegThreads = 64;
 
 // flags: bit 0 = rows of A are one vector load each, bit 1 = same for E, bit 2 = output rows
-// can be stored as one vector each (N == 4 only).
+// can be stored as one vector each (N == 4 only), bit 3 = write exp(A) to out2 transposed,
+// bit 4 = out2 rows can be stored as one vector each (N == 4 only).
+// out2 (Frechet launches only, may be null): exp(A), the value part of the pair.
 template <int N, bool Pair>
-__global__ void __launch_bounds__(kRegThreads, 8) expm_reg_kernel(View a, View e, void* __restrict__ out, int64_t batch,
-                                                       int dtype, unsigned flags) {
+__global__ void __launch_bounds__(kRegThreads, 8) expm_reg_kernel(View a, View e, void* __restrict__ out,
+                                                       void* __restrict__ out2, int64_t batch, int dtype,
+                                                       unsigned flags) {
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   RMat<N, Pair> x;
@@ -271,7 +274,10 @@ __global__ void __launch_bounds__(kRegThreads, 8) expm_reg_kernel(View a, View e
   const int64_t obase = b * (N * N);
   if (bad) {
 #pragma unroll
-    for (int t = 0; t < N * N; ++t) store_elem(out, dtype, obase + t, __int_as_float(0x7fc00000));
+    for (int t = 0; t < N * N; ++t) {
+      store_elem(out, dtype, obase + t, __int_as_float(0x7fc00000));
+      if (Pair && out2 != nullptr) store_elem(out2, dtype, obase + t, __int_as_float(0x7fc00000));
+    }
     return;
   }
   double n1 = 0.0, ninf = 0.0;
@@ -291,6 +297,24 @@ __global__ void __launch_bounds__(kRegThreads, 8) expm_reg_kernel(View a, View e
   }
   RMat<N, Pair> r = taylor<N, Pair>(m, x);
   for (int t = 0; t < s; ++t) r = rmul(r, r);
+  if constexpr (Pair) {
+    if (out2 != nullptr) {
+      const bool tr = flags & 8u;
+      float v[N * N];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = 0; j < N; ++j) v[i * N + j] = tr ? r.d[j * N + i] : r.d[i * N + j];
+      if (N == 4 && (flags & 16u)) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+          store_chunk(out2, dtype, obase + 4 * i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+      } else {
+#pragma unroll
+        for (int t = 0; t < N * N; ++t) store_elem(out2, dtype, obase + t, v[t]);
+      }
+    }
+  }
   const float* res = Pair ? r.u : r.d;
   if constexpr (N == 4) {
     if (flags & 4u) {

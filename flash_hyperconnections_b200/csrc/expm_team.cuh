@@ -53,6 +53,8 @@ enum : unsigned {
   kERows = 4u,    // direction: row chunks
   kEVec = 8u,     // direction: one vector load per chunk
   kOutVec = 16u,  // output: n % 4 == 0 and 16-byte (float32) / 8-byte (half types) aligned
+  kOut2T = 32u,   // Frechet launches with a second output: write exp(A) transposed there
+  kOut2Vec = 64u, // second output: as kOutVec
 };
 constexpr int kMaxIn = 4;
 constexpr int kMaxOut = 5;
@@ -487,9 +489,43 @@ constexpr int team_min_blocks() {
   return (228 * 1024) / smem > 16 ? 16 : (228 * 1024) / smem;
 }
 
+// The n x n matrix of plane `res` to a contiguous [batch, n, n] output, 16-byte chunks spread
+// over the team; `transposed`: element (r, c) of the output is element (c, r) of the plane.
+template <int P, int TM, int T>
+__device__ __forceinline__ void store_plane(const float* __restrict__ res, void* __restrict__ out, int dtype, int64_t b,
+                                            int n, int t, bool vec, bool transposed, bool bad) {
+  const float nanv = __int_as_float(0x7fc00000);
+#pragma unroll 1
+  for (int idx = t; idx < n * (P / 4); idx += T) {
+    const int r = idx / (P / 4);
+    const int c = 4 * (idx % (P / 4));
+    if (c >= n) continue;
+    float4 v;
+    if (transposed) {
+      v = make_float4(res[pidx<P, TM>(c, r)], res[pidx<P, TM>(c + 1, r)], res[pidx<P, TM>(c + 2, r)],
+                      res[pidx<P, TM>(c + 3, r)]);
+    } else {
+      v = *reinterpret_cast<const float4*>(res + pidx<P, TM>(r, c));
+    }
+    if (bad) v = make_float4(nanv, nanv, nanv, nanv);
+    const int64_t o = (b * n + r) * int64_t(n) + c;
+    if (vec) {
+      store_chunk(out, dtype, o, v);
+    } else {
+      const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c + u < n) store_elem(out, dtype, o + u, vals[u]);
+    }
+  }
+}
+
+// out: the result (exp(A), or L(A, E) for Frechet launches); out2 (Frechet launches only,
+// may be null): exp(A) of the same launch -- the value part of the pair -- transposed when
+// flags has kOut2T.
 template <int P, int TM, int TN, bool Pair, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
-                                                                  int64_t batch, int n, int dtype, unsigned flags) {
+                                                                  void* __restrict__ out2, int64_t batch, int n, int dtype, unsigned flags) {
   const bool a_rows = flags & kARows, a_vec = flags & kAVec;
   const bool e_rows = flags & kERows, e_vec = flags & kEVec;
   const bool out_vec = flags & kOutVec;
@@ -740,24 +776,11 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
           }
         }
       } else {
-#pragma unroll 1
-        for (int idx = t; idx < n * (P / 4); idx += T) {
-          const int r = idx / (P / 4);
-          const int c = 4 * (idx % (P / 4));
-          if (c >= n) continue;
-          float4 v = *reinterpret_cast<const float4*>(res + pidx<P, TM>(r, c));
-          if (team_bad) v = make_float4(nanv, nanv, nanv, nanv);
-          const int64_t o = (b * n + r) * int64_t(n) + c;
-          if (out_vec) {
-            store_chunk(out, dtype, o, v);
-          } else {
-            const float vals[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (c + u < n) store_elem(out, dtype, o + u, vals[u]);
-          }
-        }
+        store_plane<P, TM, T>(res, out, dtype, b, n, t, out_vec, false, team_bad);
       }
+      if (Pair && out2 != nullptr)
+        store_plane<P, TM, T>(team + cur * C::SLOT, out2, dtype, b, n, t, (flags & kOut2Vec) != 0,
+                              (flags & kOut2T) != 0, team_bad);
     }
     if (t == 0) scratch[3] = 0;  // non-finite flag: every thread read it before the steps
     team_sync<T>(tic);  // the result slot is read before the next matrix is written

@@ -72,7 +72,8 @@ int resident_blocks(Kernel kernel, LaunchShape& shape, int dev, int threads, siz
 bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
 
 template <int N, bool Pair>
-int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype, cudaStream_t stream) {
+int launch_reg(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int dtype,
+               cudaStream_t stream) {
   constexpr int threads = kRegThreads;
   const int64_t blocks = (batch + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
@@ -86,13 +87,16 @@ int launch_reg(const View& a, const View& e, void* out, int64_t batch, int dtype
   if (rows(a)) flags |= 1u;
   if (Pair && rows(e)) flags |= 2u;
   if (N == 4 && aligned(out, row_bytes)) flags |= 4u;
-  expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, batch, dtype, flags);
+  if (out2_t) flags |= 8u;
+  if (N == 4 && out2 != nullptr && aligned(out2, row_bytes)) flags |= 16u;
+  expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, out2, batch, dtype, flags);
   return cuda_status(cudaGetLastError());
 }
 
 // Load/store layout flags of the team kernel (see the enum in expm_team.cuh).
 template <int P>
-unsigned layout_flags(const View& a, const View& e, const void* out, int n, int dtype, bool pair) {
+unsigned layout_flags(const View& a, const View& e, const void* out, const void* out2, bool out2_t, int n, int dtype,
+                      bool pair) {
   unsigned f = 0;
   // Row chunks when the elements of a row are closest in memory, else column chunks; a chunk
   // is one 128-bit (float32) or 64-bit (half types) load when it is contiguous, aligned and
@@ -111,13 +115,16 @@ unsigned layout_flags(const View& a, const View& e, const void* out, int n, int 
   }
   const size_t esz = dtype == kF32 ? 4 : 2;
   if (n % 4 == 0 && aligned(out, 4 * esz)) f |= kOutVec;
+  if (out2 != nullptr && n % 4 == 0 && aligned(out2, 4 * esz)) f |= kOut2Vec;
+  if (out2_t) f |= kOut2T;
   return f;
 }
 
 // TM x TN: a thread's register tile; WARPS: warps per CTA.  A team is (P/TM) * (P/TN)
 // threads; one CTA holds WARPS * 32 / team-size teams.
 template <int P, int TM, int TN, bool Pair, int WARPS>
-int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
+int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
+                cudaStream_t stream) {
   using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int threads = WARPS * 32;
   constexpr int teams = threads / C::T;
@@ -134,16 +141,19 @@ int launch_team(const View& a, const View& e, void* out, int64_t batch, int n, i
   const int64_t items = (batch + teams - 1) / teams;
   const int64_t resident = int64_t(sms) * per_sm;
   const int blocks = int(items < resident ? items : resident);
-  kernel<<<blocks, threads, smem, stream>>>(a, e, out, batch, n, dtype, layout_flags<P>(a, e, out, n, dtype, Pair));
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, batch, n, dtype,
+                                            layout_flags<P>(a, e, out, out2, out2_t, n, dtype, Pair));
   return cuda_status(cudaGetLastError());
 }
 
+// out2 (Frechet launches only, may be null): also write exp(A) there, transposed if out2_t.
 template <bool Pair>
-int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream) {
+int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream,
+             void* out2 = nullptr, bool out2_t = false) {
   switch (n) {
-    case 2: return launch_reg<2, Pair>(a, e, out, batch, dtype, stream);
-    case 3: return launch_reg<3, Pair>(a, e, out, batch, dtype, stream);
-    case 4: return launch_reg<4, Pair>(a, e, out, batch, dtype, stream);
+    case 2: return launch_reg<2, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
+    case 3: return launch_reg<3, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
+    case 4: return launch_reg<4, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
     default: break;
   }
   // Tile shapes (TM x TN per thread) and warps per team, chosen by measurement on B200:
@@ -153,18 +163,18 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   // state per matrix).  8 x 8: 4 x 4 tiles, eight teams per warp.  16 x 16: forward 4 x 4 tiles,
   // two teams per warp; Frechet 2 x 4 tiles, one team per warp (20 % faster than 4 x 4 tiles,
   // whose 254 registers left 8 warps per SM).
-  if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, batch, n, dtype, stream);
+  if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
   if (n <= 16) {
     if constexpr (Pair) {
-      return launch_team<16, 2, 4, true, 1>(a, e, out, batch, n, dtype, stream);
+      return launch_team<16, 2, 4, true, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
     } else {
-      return launch_team<16, 4, 4, false, 1>(a, e, out, batch, n, dtype, stream);
+      return launch_team<16, 4, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
     }
   }
   if constexpr (Pair) {
-    return launch_team<32, 2, 4, true, 4>(a, e, out, batch, n, dtype, stream);
+    return launch_team<32, 2, 4, true, 4>(a, e, out, out2, out2_t, batch, n, dtype, stream);
   } else {
-    return launch_team<32, 4, 4, false, 2>(a, e, out, batch, n, dtype, stream);
+    return launch_team<32, 4, 4, false, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
   }
 }
 
@@ -215,6 +225,25 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
   return dispatch<true>(a, e, output, batch, n, dtype, static_cast<cudaStream_t>(stream));
 }
 
+int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                               const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
+                               int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
+                               int64_t batch, int32_t n, int32_t dtype, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, frechet_output);
+  if (st != FHX_OK) return st;
+  if (batch > 0 && exp_output == nullptr) return FHX_ERR_POINTER;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  st = check_view(direction, dir_s0, dir_s1, dir_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View e{direction, dir_s0, dir_s1, dir_s2, dir_negate ? -1.f : 1.f};
+  return dispatch<true>(a, e, frechet_output, batch, n, dtype, static_cast<cudaStream_t>(stream), exp_output,
+                        exp_transposed != 0);
+}
+
 const char* fhx_status_string(int32_t status) {
   switch (status) {
     case FHX_OK: return "ok";
@@ -231,6 +260,6 @@ int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda
 
 const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
 
-int32_t fhx_abi_version(void) { return 101; }
+int32_t fhx_abi_version(void) { return 102; }
 
 }  // extern "C"

@@ -29,6 +29,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/csrc/autograd/custom_function.h>
 #include <torch/csrc/autograd/forward_grad.h>
+#include <torch/csrc/autograd/python_variable.h>
+#include <torch/csrc/utils/pybind.h>
 #include <torch/library.h>
 
 #include "fhx.h"
@@ -79,6 +81,36 @@ at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
   return out;
 }
 
+// (exp(A), L(A, E)) from one launch, or with `transposed` (exp(A^T)^T, L(A, E)): the forward
+// and the backward of Y = exp(X) at A = X^T.
+std::tuple<at::Tensor, at::Tensor> run_pair(const at::Tensor& a, const at::Tensor& e, bool transposed) {
+  check_input(a);
+  TORCH_CHECK(e.sizes() == a.sizes() && e.device() == a.device() && e.scalar_type() == a.scalar_type() &&
+                  e.layout() == at::kStrided,
+              "matrix exponential direction must match the input");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const auto opts = a.options().memory_format(at::MemoryFormat::Contiguous);
+  at::Tensor y = at::empty(a.sizes(), opts);
+  at::Tensor l = at::empty(a.sizes(), opts);
+  if (a.numel() == 0) return {y, l};
+  void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
+  const int32_t status = fhx_matrix_exp_frechet(
+      a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0, e.const_data_ptr(), e.stride(0),
+      e.stride(1), e.stride(2), e.is_neg() ? 1 : 0, y.mutable_data_ptr(), transposed ? 1 : 0, l.mutable_data_ptr(),
+      a.size(0), static_cast<int32_t>(a.size(-1)), dtype_code(a), stream);
+  TORCH_CHECK(status == FHX_OK, "flash_hypercons kernel: ", fhx_status_string(status),
+              status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
+  return {y, l};
+}
+
+std::tuple<at::Tensor, at::Tensor> matrix_exp_frechet_cuda(const at::Tensor& input, const at::Tensor& direction) {
+  return run_pair(input, direction, false);
+}
+
+std::tuple<at::Tensor, at::Tensor> matrix_exp_and_grad_cuda(const at::Tensor& input, const at::Tensor& grad) {
+  return run_pair(input.mT(), grad, true);
+}
+
 at::Tensor matrix_exp_cuda(const at::Tensor& input) { return run(input, nullptr); }
 
 at::Tensor frechet_cuda(const at::Tensor& input, const at::Tensor& direction) { return run(input, &direction); }
@@ -105,10 +137,29 @@ bool has_tangent(const at::Tensor& t) {
   return false;
 }
 
-// A tensor subclass with Python dispatch (__torch_dispatch__): it must see the native
-// operators of the block formula, not this package's operator (the reference's
-// has_torch_function check, flash_hypercons/ops/matrix_exp/__init__.py:66-72).
-bool is_python_tensor(const at::Tensor& t) { return t.defined() && t.key_set().has(c10::DispatchKey::Python); }
+// A tensor subclass with Python dispatch (__torch_dispatch__) that also overrides
+// __torch_function__: it must see the native operators of the block formula, not this
+// package's operator (the reference's has_torch_function check,
+// flash_hypercons/ops/matrix_exp/__init__.py:66-72).  The tracing tensors of torch.compile
+// (FakeTensor, FunctionalTensor) carry the Python dispatch key too but disable
+// __torch_function__, so the compiled backward keeps _frechet, as in the reference.  Only
+// tensors with the Python key are inspected (under the GIL); plain tensors cost nothing.
+bool is_python_subclass(const at::Tensor& t) {
+  if (!t.defined() || !t.key_set().has(c10::DispatchKey::Python)) return false;
+  namespace py = pybind11;
+  py::gil_scoped_acquire gil;
+  try {
+    // kept for the life of the process (never destroyed after the interpreter is gone)
+    static const py::object* disabled =
+        new py::object(py::module_::import("torch._C").attr("_disabled_torch_function_impl"));
+    const auto obj = py::reinterpret_steal<py::object>(THPVariable_Wrap(t));
+    const py::object impl =
+        py::getattr(py::handle(reinterpret_cast<PyObject*>(Py_TYPE(obj.ptr()))), "__torch_function__", py::none());
+    return !impl.is_none() && !impl.is(*disabled);
+  } catch (const py::error_already_set&) {
+    return false;
+  }
+}
 
 const auto& frechet_op() {
   static const auto op = c10::Dispatcher::singleton()
@@ -187,7 +238,7 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
     const at::Tensor& grad = grads[0];
     // Forward-mode tangents need operators with forward derivatives, and tensor subclasses
     // must see native operators: the native formula.
-    if (has_tangent(input) || has_tangent(grad) || is_python_tensor(input) || is_python_tensor(grad))
+    if (has_tangent(input) || has_tangent(grad) || is_python_subclass(input) || is_python_subclass(grad))
       return {frechet_reference(input.mT(), grad)};
     // With grad mode on (a graph of this backward is being built) the call goes through the
     // autograd formula of _frechet above; otherwise straight to the kernel.
@@ -202,11 +253,18 @@ at::Tensor matrix_exp_autograd(const at::Tensor& input) { return MatrixExpFuncti
 TORCH_LIBRARY(flash_hypercons, m) {
   m.def("_matrix_exp(Tensor input) -> Tensor");
   m.def("_frechet(Tensor input, Tensor direction) -> Tensor");
+  // Extensions of this package (no reference schema): both parts of one Frechet launch.
+  // (exp(input), L(input, direction)) -- the primal and tangent of forward-mode AD.
+  m.def("_matrix_exp_frechet(Tensor input, Tensor direction) -> (Tensor, Tensor)");
+  // (exp(input), L(input^T, grad)) -- the forward and the backward of exp for a known grad.
+  m.def("_matrix_exp_and_grad(Tensor input, Tensor grad) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(flash_hypercons, CUDA, m) {
   m.impl("_matrix_exp", &matrix_exp_cuda);
   m.impl("_frechet", &frechet_cuda);
+  m.impl("_matrix_exp_frechet", &matrix_exp_frechet_cuda);
+  m.impl("_matrix_exp_and_grad", &matrix_exp_and_grad_cuda);
 }
 
 TORCH_LIBRARY_IMPL(flash_hypercons, Autograd, m) {

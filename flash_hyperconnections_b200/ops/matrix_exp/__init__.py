@@ -68,12 +68,43 @@ def _frechet_fake(input, direction):
     return _matrix_exp_fake(input)
 
 
+@torch.library.register_fake("flash_hypercons::_matrix_exp_frechet")
+def _matrix_exp_frechet_fake(input, direction):
+    _frechet_fake(input, direction)
+    return input.new_empty(input.shape), input.new_empty(input.shape)
+
+
+@torch.library.register_fake("flash_hypercons::_matrix_exp_and_grad")
+def _matrix_exp_and_grad_fake(input, grad):
+    _frechet_fake(input, grad)
+    return input.new_empty(input.shape), input.new_empty(input.shape)
+
+
 def _has_tangent(t) -> bool:
     # Outside every forward-AD level no tensor can carry a tangent; unpack_dual would
     # return None, so the (comparatively slow) call is skipped.
     if torch.autograd.forward_ad._current_level < 0:
         return False
     return torch.autograd.forward_ad.unpack_dual(t).tangent is not None
+
+
+def _jvp_through_kernel(input: torch.Tensor):
+    """Forward-mode AD of exp on the kernel: primal exp(A) and tangent L(A, E) from one launch
+    of the Frechet kernel (``_matrix_exp_frechet``).  Taken for a plain dual tensor in pure
+    forward mode -- neither primal nor tangent needs a reverse-mode graph and no torch.func
+    transform is active -- on an eligible input; returns None otherwise (the caller then uses
+    native operators, as the reference does for every forward-AD input,
+    flash_hypercons/ops/matrix_exp/__init__.py:89-94)."""
+    if type(input) is not torch.Tensor or torch._C._are_functorch_transforms_active():
+        return None
+    primal, tangent = torch.autograd.forward_ad.unpack_dual(input)
+    if tangent is None or primal.requires_grad or tangent.requires_grad or not _eligible(primal):
+        return None
+    if (type(tangent) is not torch.Tensor or tangent._is_zerotensor() or tangent.layout != torch.strided
+            or tangent.shape != primal.shape or tangent.dtype != primal.dtype or tangent.device != primal.device):
+        return None
+    y, ty = torch.ops.flash_hypercons._matrix_exp_frechet(primal, tangent)
+    return torch.autograd.forward_ad.make_dual(y, ty)
 
 
 def matrix_exp(input: torch.Tensor) -> torch.Tensor:
@@ -91,10 +122,38 @@ def matrix_exp(input: torch.Tensor) -> torch.Tensor:
         or torch._C._are_functorch_transforms_active()
         or _has_tangent(input)
     ):
+        # Extension: pure forward-mode AD of a plain tensor runs on the Frechet kernel.
+        if _has_tangent(input):
+            fused = _jvp_through_kernel(input)
+            if fused is not None:
+                return fused
         return _native(input, promote=True)
     if not _eligible(input):
         return _native(input)
     return torch.ops.flash_hypercons._matrix_exp(input)
+
+
+def matrix_exp_and_grad(input: torch.Tensor, grad_output: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Forward and backward of ``Y = exp(input)`` in one kernel launch, for a known upstream
+    gradient: returns ``(Y, dL/dinput)`` with ``dL/dinput = L(input^T, grad_output)``, the
+    gradient ``torch.autograd.grad(matrix_exp(input), input, grad_output)`` computes.
+
+    Eligible inputs (as for ``matrix_exp``) run one launch of the Frechet kernel, which
+    carries exp(input^T) through its program anyway and stores it transposed.  The results are
+    not attached to an autograd graph.  Other inputs use native PyTorch operators.
+    (Extension of this package: the reference has no single call for this.)
+    """
+    if (isinstance(input, torch.Tensor) and type(input) in (torch.Tensor, torch.nn.Parameter)
+            and type(grad_output) is torch.Tensor and _eligible(input)
+            and not torch._C._are_functorch_transforms_active()
+            and grad_output.shape == input.shape and grad_output.dtype == input.dtype
+            and grad_output.device == input.device and grad_output.layout == torch.strided):
+        return torch.ops.flash_hypercons._matrix_exp_and_grad(input.detach(), grad_output.detach())
+    with torch.enable_grad():
+        x = input.detach().requires_grad_()
+        y = _native(x, promote=True)
+        (grad,) = torch.autograd.grad(y, x, grad_output)
+    return y.detach(), grad
 
 
 class _MatrixExpMode(TorchFunctionMode):
@@ -122,4 +181,4 @@ def use_backend() -> TorchFunctionMode:
     return _MatrixExpMode()
 
 
-__all__ = ["matrix_exp", "use_backend"]
+__all__ = ["matrix_exp", "matrix_exp_and_grad", "use_backend"]

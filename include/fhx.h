@@ -68,6 +68,29 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
                     const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
                     void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
 
+/*
+ * exp(A) and L(A, E) from ONE launch: the Frechet kernel carries the pair (exp, derivative)
+ * through its program anyway, and this entry point stores both parts.
+ *   exp_output       contiguous [batch, n, n]: exp(A), or exp(A)^T = exp(A^T) when
+ *                    exp_transposed is non-zero
+ *   frechet_output   contiguous [batch, n, n]: L(A, E)
+ * Two uses:
+ *   - forward-mode AD (JVP) of exp at A with tangent E: primal exp(A) and tangent L(A, E);
+ *   - forward and backward of Y = exp(X) together, when the upstream gradient G is known:
+ *     pass A = X^T (in_s1/in_s2 swapped), E = G, exp_transposed = 1; then
+ *     exp_output = exp(X) = Y and frechet_output = L(X^T, G) = dL/dX.
+ * The pair's degree and scaling are those of fhx_frechet on the same A, so frechet_output
+ * equals fhx_frechet's output bit for bit; exp_output can differ from fhx_matrix_exp's in
+ * the last bits where the forward kernel shares a degree between neighbouring matrices.
+ * Reference counterpart: none as one call.  It fuses the forward-AD rule of the reference
+ * (native, flash_hypercons/ops/matrix_exp/__init__.py:89-94) and the forward + backward pair
+ * _matrix_exp / _frechet (csrc/register.cpp:11-12) into one launch.
+ */
+int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                               const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
+                               int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
+                               int64_t batch, int32_t n, int32_t dtype, void* stream);
+
 /* Static description of a status code. */
 const char* fhx_status_string(int32_t status);
 
