@@ -192,6 +192,56 @@ __device__ __forceinline__ RMat<N, Pair> taylor(int m, const RMat<N, Pair>& a) {
   return r;
 }
 
+// exp of one n x n matrix held in registers -- with Pair, the pair (A, E) -> (exp(A), L(A, E))
+// -- by the arithmetic of expm_reg_kernel below: float64 norms summed in the same order, the
+// same (m, s), scaling, scheme and squarings.  Any non-finite entry makes both parts NaN.
+// Used by the fused kernels that apply exp to other data (stream_mix.cuh).
+template <int N, bool Pair>
+__device__ __forceinline__ RMat<N, Pair> expm_regs(RMat<N, Pair> x) {
+  bool bad = false;
+  double col[N], row[N];
+#pragma unroll
+  for (int t = 0; t < N; ++t) col[t] = row[t] = 0.0;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = x.d[i * N + j];
+      bad |= !isfinite(v);
+      const double av = fabs(double(v));
+      col[j] += av;
+      row[i] += av;
+      if constexpr (Pair) bad |= !isfinite(x.u[i * N + j]);
+    }
+  if (bad) {
+    RMat<N, Pair> r;
+#pragma unroll
+    for (int t = 0; t < N * N; ++t) {
+      r.d[t] = __int_as_float(0x7fc00000);
+      if constexpr (Pair) r.u[t] = __int_as_float(0x7fc00000);
+    }
+    return r;
+  }
+  double n1 = 0.0, ninf = 0.0;
+#pragma unroll
+  for (int t = 0; t < N; ++t) {
+    n1 = fmax(n1, col[t]);
+    ninf = fmax(ninf, row[t]);
+  }
+  int m, s;
+  choose_degree(fmin(n1, ninf), &m, &s);
+  if (s > 0) {
+#pragma unroll
+    for (int t = 0; t < N * N; ++t) {
+      x.d[t] = scale_pow2(x.d[t], s);
+      if constexpr (Pair) x.u[t] = scale_pow2(x.u[t], s);
+    }
+  }
+  RMat<N, Pair> r = taylor<N, Pair>(m, x);
+  for (int t = 0; t < s; ++t) r = rmul(r, r);
+  return r;
+}
+
 // Row i of matrix b of a view as four elements (N == 4, row contiguous and aligned): one
 // 128-bit (float32) or 64-bit (half types) load.
 __device__ __forceinline__ float4 load_row4(const View& v, int dtype, int64_t off) {

@@ -137,28 +137,42 @@ bool has_tangent(const at::Tensor& t) {
   return false;
 }
 
-// A tensor subclass with Python dispatch (__torch_dispatch__) that also overrides
-// __torch_function__: it must see the native operators of the block formula, not this
-// package's operator (the reference's has_torch_function check,
-// flash_hypercons/ops/matrix_exp/__init__.py:66-72).  The tracing tensors of torch.compile
-// (FakeTensor, FunctionalTensor) carry the Python dispatch key too but disable
-// __torch_function__, so the compiled backward keeps _frechet, as in the reference.  Only
-// tensors with the Python key are inspected (under the GIL); plain tensors cost nothing.
-bool is_python_subclass(const at::Tensor& t) {
-  if (!t.defined() || !t.key_set().has(c10::DispatchKey::Python)) return false;
+// A tensor subclass that overrides __torch_function__ (the reference's has_torch_function
+// check, flash_hypercons/ops/matrix_exp/__init__.py:66-72).  The reference then computes the
+// gradient with the native block formula in Python, so the subclass sees every operator and
+// the gradient comes back as the subclass.  Plain tensors (no Python object, or exactly
+// torch.Tensor / Parameter) are recognised without the GIL.  Subclasses whose
+// __torch_function__ is disabled -- __torch_dispatch__ subclasses, and the tracing tensors of
+// torch.compile (FakeTensor, FunctionalTensor) -- do not count, as in the reference: they keep
+// _frechet.
+bool overrides_torch_function(const at::Tensor& t) {
+  if (!t.defined()) return false;
+  PyObject* obj = t.unsafeGetTensorImpl()->pyobj_slot()->load_pyobj();
+  if (obj == nullptr || THPVariable_CheckTypeExact(Py_TYPE(obj))) return false;
   namespace py = pybind11;
   py::gil_scoped_acquire gil;
   try {
     // kept for the life of the process (never destroyed after the interpreter is gone)
     static const py::object* disabled =
         new py::object(py::module_::import("torch._C").attr("_disabled_torch_function_impl"));
-    const auto obj = py::reinterpret_steal<py::object>(THPVariable_Wrap(t));
     const py::object impl =
-        py::getattr(py::handle(reinterpret_cast<PyObject*>(Py_TYPE(obj.ptr()))), "__torch_function__", py::none());
+        py::getattr(py::handle(reinterpret_cast<PyObject*>(Py_TYPE(obj))), "__torch_function__", py::none());
     return !impl.is_none() && !impl.is(*disabled);
   } catch (const py::error_already_set&) {
     return false;
   }
+}
+
+// The native block formula called through Python (flash_hyperconnections_b200.ops.matrix_exp.
+// _frechet_reference), so that __torch_function__ subclasses see its operators.
+at::Tensor frechet_reference_python(const at::Tensor& input, const at::Tensor& direction) {
+  namespace py = pybind11;
+  py::gil_scoped_acquire gil;
+  static const py::object* fn = new py::object(
+      py::module_::import("flash_hyperconnections_b200.ops.matrix_exp").attr("_frechet_reference"));
+  const py::object out = (*fn)(py::reinterpret_steal<py::object>(THPVariable_Wrap(input)),
+                               py::reinterpret_steal<py::object>(THPVariable_Wrap(direction)));
+  return THPVariable_Unpack(out.ptr());
 }
 
 const auto& frechet_op() {
@@ -236,10 +250,12 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
                                                  torch::autograd::variable_list grads) {
     const at::Tensor input = ctx->get_saved_variables()[0];
     const at::Tensor& grad = grads[0];
-    // Forward-mode tangents need operators with forward derivatives, and tensor subclasses
-    // must see native operators: the native formula.
-    if (has_tangent(input) || has_tangent(grad) || is_python_subclass(input) || is_python_subclass(grad))
-      return {frechet_reference(input.mT(), grad)};
+    // Tensor subclasses that override __torch_function__ see the native formula's operators
+    // in Python; forward-mode tangents need operators with forward derivatives: the native
+    // formula.
+    if (overrides_torch_function(input) || overrides_torch_function(grad))
+      return {frechet_reference_python(input.mT(), grad)};
+    if (has_tangent(input) || has_tangent(grad)) return {frechet_reference(input.mT(), grad)};
     // With grad mode on (a graph of this backward is being built) the call goes through the
     // autograd formula of _frechet above; otherwise straight to the kernel.
     return {frechet_op().call(input.mT(), grad)};

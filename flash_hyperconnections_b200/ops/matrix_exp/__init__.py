@@ -45,6 +45,18 @@ def _native(input: torch.Tensor, *, promote: bool = False) -> torch.Tensor:
     return _NATIVE(input)
 
 
+def _frechet_reference(input: torch.Tensor, direction: torch.Tensor) -> torch.Tensor:
+    """Differentiable L(input, direction): the upper-right block of the native float32
+    exponential of [[A, E], [0, A]], cast back (reference __init__.py:32-37).  The C++ backward
+    calls it for tensor subclasses that override __torch_function__, so that they see these
+    operators."""
+    n = input.shape[-1]
+    a = input.float()
+    e = direction.float()
+    block = torch.cat((torch.cat((a, e), -1), torch.cat((torch.zeros_like(a), a), -1)), -2)
+    return torch.linalg.matrix_exp(block)[..., :n, n:].to(input.dtype)
+
+
 @torch.library.register_fake("flash_hypercons::_matrix_exp")
 def _matrix_exp_fake(input):
     # Same metadata checks as the reference fake (__init__.py:40-49).

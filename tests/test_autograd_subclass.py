@@ -1,9 +1,11 @@
-"""Tensor subclasses with Python dispatch in the backward of fh.matrix_exp.
+"""Tensor subclasses in the backward of fh.matrix_exp.
 
-The original package's backward checks ``has_torch_function((input, grad_output))`` and then
-computes the gradient with native operators (flash_hypercons/ops/matrix_exp/__init__.py:66-72),
-so a ``__torch_dispatch__`` subclass passed as the incoming gradient sees only native aten
-operators and the gradient comes back as that subclass.  Same here.
+The original package's backward checks ``has_torch_function((input, grad_output))`` and, for a
+subclass that overrides ``__torch_function__``, computes the gradient with the native block
+formula in Python, so that the subclass sees those operators and the gradient comes back as the
+subclass (flash_hypercons/ops/matrix_exp/__init__.py:66-72).  Subclasses whose
+``__torch_function__`` is disabled (``__torch_dispatch__`` subclasses) keep the package's
+``_frechet`` operator there, and so they do here.
 """
 
 import pytest
@@ -13,11 +15,17 @@ from torch.utils._pytree import tree_map
 import flash_hypercons as fh
 from oracle import expm_oracle as O
 
+from .test_routing import op_names
+
 pytestmark = pytest.mark.gpu
 
 
+class Tagged(torch.Tensor):
+    """A __torch_function__ subclass: every operator result is a Tagged."""
+
+
 class RecordingTensor(torch.Tensor):
-    """Wrapper subclass that records every aten operator it sees."""
+    """Wrapper subclass (__torch_dispatch__) that records every operator it sees."""
 
     seen: list = []
 
@@ -37,14 +45,28 @@ class RecordingTensor(torch.Tensor):
         return tree_map(wrap, func(*tree_map(unwrap, args), **tree_map(unwrap, kwargs or {})))
 
 
-def test_subclass_gradient_takes_native_formula():
+def test_torch_function_subclass_gradient_takes_native_formula():
+    a = (torch.randn(6, 5, 5, device="cuda") * 0.5).requires_grad_()
+    g = torch.randn(6, 5, 5, device="cuda")
+    y = fh.matrix_exp(a)
+    (grad,), names = op_names(lambda: torch.autograd.grad(y, a, g.as_subclass(Tagged)))
+    assert type(grad) is Tagged
+    assert "flash_hypercons::_frechet" not in names
+    err = O.per_matrix_error(grad.as_subclass(torch.Tensor), O.frechet_fp64(a.detach().mT, g)).max()
+    assert err <= O.tolerance("float32", True), err
+    # plain gradients keep the kernel
+    y = fh.matrix_exp(a)
+    _, names = op_names(lambda: torch.autograd.grad(y, a, g))
+    assert "flash_hypercons::_frechet" in names
+
+
+def test_dispatch_subclass_gradient_keeps_frechet_operator():
     a = (torch.randn(6, 5, 5, device="cuda") * 0.5).requires_grad_()
     g = torch.randn(6, 5, 5, device="cuda")
     y = fh.matrix_exp(a)
     RecordingTensor.seen = []
     (grad,) = torch.autograd.grad(y, a, RecordingTensor(g))
     assert isinstance(grad, RecordingTensor)
-    assert not any("flash_hypercons" in name for name in RecordingTensor.seen), RecordingTensor.seen
-    assert any("matrix_exp" in name for name in RecordingTensor.seen)
+    assert any("flash_hypercons._frechet" in name for name in RecordingTensor.seen), RecordingTensor.seen
     err = O.per_matrix_error(grad.elem, O.frechet_fp64(a.detach().mT, g)).max()
     assert err <= O.tolerance("float32", True), err
