@@ -66,7 +66,7 @@ def build_libfhx(force: bool = False, verbose: bool = False, extra_flags=()) -> 
     cmd = [
         _nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
         "-Xcompiler", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{CSRC}", *extra_flags,
-        "-o", tmp, CSRC / "fhx_expm.cu",
+        "-o", tmp, *sorted(CSRC.glob("*.cu")),
     ]
     _run(cmd, verbose)
     os.replace(tmp, LIBFHX)

@@ -13,6 +13,11 @@ namespace fhx {
 
 enum : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
+// The CUDA error behind the calling thread's last FHX_ERR_CUDA (fhx_last_cuda_error), and the
+// status of a CUDA runtime result that remembers a failure there (both in fhx_expm.cu).
+extern thread_local cudaError_t g_last_cuda_error;
+int cuda_status(cudaError_t err);
+
 // A read-only strided [batch, n, n] view; `sign` is -1 for a lazily negated tensor.
 struct View {
   const void* data;

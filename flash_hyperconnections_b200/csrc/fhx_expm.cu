@@ -15,6 +15,15 @@
 #include "fhx.h"
 
 namespace fhx {
+
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+int cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return FHX_OK;
+  g_last_cuda_error = err;
+  return FHX_ERR_CUDA;
+}
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -27,15 +36,6 @@ struct DeviceInfo {
 std::mutex g_mutex;
 DeviceInfo g_devices[kMaxDevices];
 
-// The CUDA error behind the calling thread's last FHX_ERR_CUDA.
-thread_local cudaError_t g_last_cuda_error = cudaSuccess;
-
-// Status of a CUDA runtime result; a failure is remembered for fhx_last_cuda_error().
-int cuda_status(cudaError_t err) {
-  if (err == cudaSuccess) return FHX_OK;
-  g_last_cuda_error = err;
-  return FHX_ERR_CUDA;
-}
 
 // Per-(kernel, device) launch geometry: resident CTAs per SM at the kernel's smem size.
 struct LaunchShape {

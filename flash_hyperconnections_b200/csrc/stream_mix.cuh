@@ -22,6 +22,9 @@
 // hyper-connections, README.md:1-5).
 #pragma once
 
+#include <cstring>
+#include <type_traits>
+
 #include "expm_common.cuh"
 #include "expm_reg.cuh"
 
@@ -59,7 +62,7 @@ struct HalfChunk {
   __device__ static float2 to_f2(unsigned w) {
     H2 h;
     memcpy(&h, &w, 4);
-    if constexpr (sizeof(HT) == 2 && std::is_same<HT, __nv_bfloat16>::value) return __bfloat1622float2(h);
+    if constexpr (std::is_same<HT, __nv_bfloat16>::value) return __bfloat1622float2(h);
     else return __half22float2(h);
   }
   __device__ static unsigned from_f2(float a, float b) {

@@ -42,6 +42,7 @@ extern "C" {
                                 cudaError_t is kept for fhx_last_cuda_error()            */
 
 #define FHX_MAX_N 32
+#define FHX_MIX_MAX_N 4      /* streams per token of the fused stream mixing            */
 
 /*
  * Y = exp(A) for a batch of n x n matrices, 2 <= n <= 32.
@@ -90,6 +91,40 @@ int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, 
                                const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
                                int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
                                int64_t batch, int32_t n, int32_t dtype, void* stream);
+
+/*
+ * Hyper-connection stream mixing fused with the exponential, one warp per token:
+ *   Y[t] = exp(H[t]) X[t]
+ * for tokens t < `tokens`, H[t] an n x n mixing matrix (2 <= n <= FHX_MIX_MAX_N) and X[t] the
+ * token's n residual streams of width d.
+ *   h               H, element (t, i, j) at h[t*h_s0 + i*h_s1 + j*h_s2] in h_dtype;
+ *                   h_negate non-zero: use -H
+ *   x               X, element (t, j, c) at x[t*x_s0 + j*x_s1 + c] in x_dtype (unit column stride)
+ *   y               contiguous [tokens, n, d] in x_dtype
+ * exp(H[t]) is computed in registers with the arithmetic of fhx_matrix_exp's n <= 4 kernel and
+ * never written to memory; a non-finite entry of H[t] makes Y[t] NaN.  Rows move in 16-byte
+ * chunks when d and the row strides allow it.
+ * Reference counterpart: none (the reference computes exp only; its name refers to
+ * hyper-connections, README.md:1-5).  Unfused, this is fhx_matrix_exp followed by a batched
+ * [n x n] x [n x d] product reading exp(H) back from memory.
+ */
+int32_t fhx_stream_mix(const void* h, int64_t h_s0, int64_t h_s1, int64_t h_s2, int32_t h_negate, int32_t h_dtype,
+                       const void* x, int64_t x_s0, int64_t x_s1, int32_t x_dtype, void* y, int64_t tokens, int32_t n,
+                       int64_t d, void* stream);
+
+/*
+ * Backward of fhx_stream_mix for the upstream gradient dY (x_dtype, element (t, i, c) at
+ * dy[t*dy_s0 + i*dy_s1 + c]):
+ *   dX[t] = exp(H[t])^T dY[t]                 dx: contiguous [tokens, n, d] in x_dtype
+ *   dH[t] = L(H[t]^T, dY[t] X[t]^T)           dh: contiguous [tokens, n, n] in h_dtype
+ * exp(H[t]) is recomputed in registers, dY[t] X[t]^T is reduced over d in float32 in a fixed
+ * order (deterministic), and the Frechet derivative runs in registers with the arithmetic of
+ * fhx_frechet's n <= 4 kernel.
+ */
+int32_t fhx_stream_mix_backward(const void* h, int64_t h_s0, int64_t h_s1, int64_t h_s2, int32_t h_negate,
+                                int32_t h_dtype, const void* x, int64_t x_s0, int64_t x_s1, int32_t x_dtype,
+                                const void* dy, int64_t dy_s0, int64_t dy_s1, void* dx, void* dh, int64_t tokens,
+                                int32_t n, int64_t d, void* stream);
 
 /* Static description of a status code. */
 const char* fhx_status_string(int32_t status);
