@@ -467,6 +467,68 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
 
 
 # ----------------------------------------------------------------------------------------
+# hyper-connection stream mixing (config 2's mixing matrices applied to residual streams)
+# ----------------------------------------------------------------------------------------
+MIX_TOKENS = 65536   # config 2: 16 sequences x 4096 tokens
+MIX_STREAMS = 4
+MIX_WIDTH = 4096     # residual stream width D (model dimension)
+
+
+def measure_stream_mix(fh, dist, steps, warmup, device):
+    """fwd+bwd of Y = exp(H) X per token: the fused kernels (fh.mix_streams) against the unfused
+    composition (fh.matrix_exp, then a batched matmul, with autograd through both), bf16, on
+    this rank's shard of the tokens.  Inputs are larger than L2."""
+    W = workloads_module()
+    cfg = W.CONFIGS[2]
+    tokens = MIX_TOKENS // dist.world
+    start = dist.rank * tokens
+    h, _ = W.generate(cfg, start, tokens, device=device)
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(90412 + dist.rank)
+    x = torch.randn((tokens, MIX_STREAMS, MIX_WIDTH), generator=gen).to(torch.bfloat16).to(device)
+    dy = torch.randn((tokens, MIX_STREAMS, MIX_WIDTH), generator=gen).to(torch.bfloat16).to(device)
+
+    def fused():
+        hh = h.detach().requires_grad_()
+        xx = x.detach().requires_grad_()
+        y = fh.mix_streams(hh, xx)
+        torch.autograd.grad(y, (xx, hh), dy)
+
+    def unfused():
+        hh = h.detach().requires_grad_()
+        xx = x.detach().requires_grad_()
+        y = fh.matrix_exp(hh) @ xx
+        torch.autograd.grad(y, (xx, hh), dy)
+
+    out = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = dist.max(e0.elapsed_time(e1) / steps)
+    elt = 2
+    per_token = 5 * MIX_STREAMS * MIX_WIDTH * elt + 3 * MIX_STREAMS**2 * elt  # X, Y, X, dY, dX; H, H, dH
+    hbm = per_token * tokens / (out["fused"] * 1e6)
+    del h, x, dy
+    torch.cuda.empty_cache()
+    return {
+        "workload": f"bf16 H [{MIX_TOKENS}, {MIX_STREAMS}, {MIX_STREAMS}] (config 2 generators) applied to streams "
+                    f"[{MIX_TOKENS}, {MIX_STREAMS}, {MIX_WIDTH}]; fwd + bwd (d streams, d H)",
+        "value": MIX_TOKENS / (out["fused"] / 1e3), "unit": "tokens/s", "ms_per_step": out["fused"],
+        "unfused_ms_per_step": out["unfused"], "speedup_vs_unfused": out["unfused"] / out["fused"],
+        "hbm": {"algorithmic_bytes_per_token": per_token, "achieved_gbs_per_gpu": hbm},
+        "unfused": "fh.matrix_exp(H) @ X with autograd (exp launch, batched matmul, Frechet launch, matmul backward)",
+    }
+
+
+# ----------------------------------------------------------------------------------------
 # CPU path of the reference (native torch + autograd on the host cores)
 # ----------------------------------------------------------------------------------------
 def cpu_reference_sample(cfg, target_seconds: float):
@@ -619,6 +681,9 @@ def main():
                     "matches_eager": r["graph_matches_eager"],
                     "path": "one fwd+bwd step (fh.matrix_exp + autograd.grad) captured in torch.cuda.CUDAGraph, replayed",
                 }
+    stream_mix = None
+    if not args.no_extras:
+        stream_mix = measure_stream_mix(fh, dist, max(5, args.steps), args.warmup, device)
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_extras:
         cpu = cpu_reference_sample(cfg, args.cpu_seconds)
@@ -685,6 +750,11 @@ def main():
             line["cpu_baseline"] = {k: v for k, v in cpu.items() if k != "seconds"}
         if extras:
             line["secondary_configs"] = extras
+        if stream_mix:
+            peak_hbm = float(peaks.get("hbm_gbs", 6650.0))
+            stream_mix["hbm"]["peak_gbs"] = peak_hbm
+            stream_mix["hbm"]["frac"] = stream_mix["hbm"]["achieved_gbs_per_gpu"] / peak_hbm
+            line["stream_mix"] = stream_mix
         print(json.dumps(line), flush=True)
     dist.close()
 

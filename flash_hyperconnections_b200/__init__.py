@@ -11,7 +11,7 @@ from ._native import load_extension as _load_extension
 
 _C = _load_extension()
 
-from .ops.matrix_exp import matrix_exp, matrix_exp_and_grad, use_backend  # noqa: E402
+from .ops.matrix_exp import matrix_exp, matrix_exp_and_grad, mix_streams, use_backend  # noqa: E402
 
 __version__ = "0.1.0"
-__all__ = ["matrix_exp", "matrix_exp_and_grad", "use_backend"]
+__all__ = ["matrix_exp", "matrix_exp_and_grad", "mix_streams", "use_backend"]

@@ -39,6 +39,11 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_frechet.restype = i32
     lib.fhx_matrix_exp_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i32, vp, i64, i32, i32, vp]
     lib.fhx_matrix_exp_frechet.restype = i32
+    lib.fhx_stream_mix.argtypes = [vp, i64, i64, i64, i32, i32, vp, i64, i64, i32, vp, i64, i32, i64, vp]
+    lib.fhx_stream_mix.restype = i32
+    lib.fhx_stream_mix_backward.argtypes = [vp, i64, i64, i64, i32, i32, vp, i64, i64, i32, vp, i64, i64, vp, vp,
+                                            i64, i32, i64, vp]
+    lib.fhx_stream_mix_backward.restype = i32
     lib.fhx_status_string.argtypes = [i32]
     lib.fhx_status_string.restype = ctypes.c_char_p
     lib.fhx_abi_version.argtypes = []

@@ -25,6 +25,7 @@
 #include <ATen/ops/cat.h>
 #include <ATen/ops/empty.h>
 #include <ATen/ops/linalg_matrix_exp.h>
+#include <ATen/ops/matmul.h>
 #include <ATen/ops/zeros_like.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/csrc/autograd/custom_function.h>
@@ -264,6 +265,110 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
 
 at::Tensor matrix_exp_autograd(const at::Tensor& input) { return MatrixExpFunction::apply(input); }
 
+// ---- hyper-connection stream mixing: Y = exp(H) X per token (fhx_stream_mix) ----
+
+void check_mix(const at::Tensor& h, const at::Tensor& x) {
+  auto ok = [](const at::Tensor& t) {
+    return t.scalar_type() == at::kFloat || t.scalar_type() == at::kHalf || t.scalar_type() == at::kBFloat16;
+  };
+  TORCH_CHECK(h.is_cuda() && x.is_cuda() && h.device() == x.device() && h.layout() == at::kStrided &&
+                  x.layout() == at::kStrided && h.dim() == 3 && x.dim() == 3 && h.size(1) == h.size(2) &&
+                  h.size(1) >= 2 && h.size(1) <= FHX_MIX_MAX_N && x.size(0) == h.size(0) && x.size(1) == h.size(1) &&
+                  ok(h) && ok(x),
+              "expected CUDA tensors h [T, n, n] (2 <= n <= 4) and streams [T, n, D] on one device, in float32, "
+              "float16, or bfloat16");
+}
+
+// Streams with a unit column stride and no lazy negation (the kernels' layout); a copy otherwise.
+at::Tensor unit_columns(const at::Tensor& x) {
+  at::Tensor r = x.is_neg() ? x.resolve_neg() : x;
+  return (r.size(2) <= 1 || r.stride(2) == 1) ? r : r.contiguous();
+}
+
+at::Tensor mix_streams_cuda(const at::Tensor& h, const at::Tensor& x) {
+  check_mix(h, x);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const at::Tensor xs = unit_columns(x);
+  at::Tensor y = at::empty(x.sizes(), x.options().memory_format(at::MemoryFormat::Contiguous));
+  if (y.numel() == 0) return y;
+  void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
+  const int32_t status = fhx_stream_mix(h.const_data_ptr(), h.stride(0), h.stride(1), h.stride(2), h.is_neg() ? 1 : 0,
+                                        dtype_code(h), xs.const_data_ptr(), xs.stride(0), xs.stride(1), dtype_code(xs),
+                                        y.mutable_data_ptr(), h.size(0), static_cast<int32_t>(h.size(1)), x.size(2),
+                                        stream);
+  TORCH_CHECK(status == FHX_OK, "flash_hypercons stream mixing: ", fhx_status_string(status),
+              status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
+  return y;
+}
+
+std::tuple<at::Tensor, at::Tensor> mix_streams_backward_cuda(const at::Tensor& h, const at::Tensor& x,
+                                                             const at::Tensor& grad) {
+  check_mix(h, x);
+  TORCH_CHECK(grad.sizes() == x.sizes() && grad.device() == x.device() && grad.scalar_type() == x.scalar_type() &&
+                  grad.layout() == at::kStrided,
+              "stream mixing gradient must match the streams");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const at::Tensor xs = unit_columns(x);
+  const at::Tensor gs = unit_columns(grad);
+  at::Tensor dx = at::empty(x.sizes(), x.options().memory_format(at::MemoryFormat::Contiguous));
+  at::Tensor dh = at::empty(h.sizes(), h.options().memory_format(at::MemoryFormat::Contiguous));
+  if (dh.numel() == 0) return {dx, dh};
+  void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
+  const int32_t status = fhx_stream_mix_backward(
+      h.const_data_ptr(), h.stride(0), h.stride(1), h.stride(2), h.is_neg() ? 1 : 0, dtype_code(h),
+      xs.const_data_ptr(), xs.stride(0), xs.stride(1), dtype_code(xs), gs.const_data_ptr(), gs.stride(0), gs.stride(1),
+      dx.mutable_data_ptr(), dh.mutable_data_ptr(), h.size(0), static_cast<int32_t>(h.size(1)), x.size(2), stream);
+  TORCH_CHECK(status == FHX_OK, "flash_hypercons stream mixing backward: ", fhx_status_string(status),
+              status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
+  return {dx, dh};
+}
+
+// Differentiable native formula of the backward (float32 math, cast back): used when a graph
+// of the backward is built, for forward-mode tangents and for __torch_function__ subclasses.
+std::tuple<at::Tensor, at::Tensor> mix_streams_backward_native(const at::Tensor& h, const at::Tensor& x,
+                                                               const at::Tensor& grad) {
+  const at::Tensor hf = h.to(at::kFloat), xf = x.to(at::kFloat), gf = grad.to(at::kFloat);
+  const at::Tensor e = at::linalg_matrix_exp(hf);
+  const at::Tensor dx = at::matmul(e.mT(), gf).to(x.scalar_type());
+  const at::Tensor dh = frechet_reference(h.mT(), at::matmul(gf, xf.mT()));
+  return {dx, dh};
+}
+
+struct MixStreamsFunction : public torch::autograd::Function<MixStreamsFunction> {
+  static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& h, const at::Tensor& x) {
+    static const auto op = c10::Dispatcher::singleton()
+                               .findSchemaOrThrow("flash_hypercons::_mix_streams", "")
+                               .typed<at::Tensor(const at::Tensor&, const at::Tensor&)>();
+    at::Tensor out;
+    {
+      at::AutoDispatchBelowADInplaceOrView below;
+      out = op.call(h, x);
+    }
+    ctx->save_for_backward({h, x});
+    return out;
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    static const auto op = c10::Dispatcher::singleton()
+                               .findSchemaOrThrow("flash_hypercons::_mix_streams_backward", "")
+                               .typed<std::tuple<at::Tensor, at::Tensor>(const at::Tensor&, const at::Tensor&,
+                                                                         const at::Tensor&)>();
+    const auto saved = ctx->get_saved_variables();
+    const at::Tensor& h = saved[0];
+    const at::Tensor& x = saved[1];
+    const at::Tensor& grad = grads[0];
+    if (!grad.defined()) return {at::Tensor(), at::Tensor()};
+    const bool native = at::GradMode::is_enabled() || has_tangent(h) || has_tangent(x) || has_tangent(grad) ||
+                        overrides_torch_function(h) || overrides_torch_function(x) || overrides_torch_function(grad);
+    at::Tensor dx, dh;
+    std::tie(dx, dh) = native ? mix_streams_backward_native(h, x, grad) : op.call(h, x, grad);
+    return {ctx->needs_input_grad(0) ? dh : at::Tensor(), ctx->needs_input_grad(1) ? dx : at::Tensor()};
+  }
+};
+
+at::Tensor mix_streams_autograd(const at::Tensor& h, const at::Tensor& x) { return MixStreamsFunction::apply(h, x); }
+
 }  // namespace
 
 TORCH_LIBRARY(flash_hypercons, m) {
@@ -274,6 +379,10 @@ TORCH_LIBRARY(flash_hypercons, m) {
   m.def("_matrix_exp_frechet(Tensor input, Tensor direction) -> (Tensor, Tensor)");
   // (exp(input), L(input^T, grad)) -- the forward and the backward of exp for a known grad.
   m.def("_matrix_exp_and_grad(Tensor input, Tensor grad) -> (Tensor, Tensor)");
+  // exp(h) @ streams per token (hyper-connection stream mixing), and its backward
+  // (d streams, d h).
+  m.def("_mix_streams(Tensor h, Tensor streams) -> Tensor");
+  m.def("_mix_streams_backward(Tensor h, Tensor streams, Tensor grad) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(flash_hypercons, CUDA, m) {
@@ -281,11 +390,14 @@ TORCH_LIBRARY_IMPL(flash_hypercons, CUDA, m) {
   m.impl("_frechet", &frechet_cuda);
   m.impl("_matrix_exp_frechet", &matrix_exp_frechet_cuda);
   m.impl("_matrix_exp_and_grad", &matrix_exp_and_grad_cuda);
+  m.impl("_mix_streams", &mix_streams_cuda);
+  m.impl("_mix_streams_backward", &mix_streams_backward_cuda);
 }
 
 TORCH_LIBRARY_IMPL(flash_hypercons, Autograd, m) {
   m.impl("_matrix_exp", &matrix_exp_autograd);
   m.impl("_frechet", &frechet_autograd);
+  m.impl("_mix_streams", &mix_streams_autograd);
 }
 
 static PyModuleDef module_def = {PyModuleDef_HEAD_INIT, "_C", "flash_hypercons operator registration", -1,

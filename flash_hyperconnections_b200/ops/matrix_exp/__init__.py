@@ -22,6 +22,7 @@ _NATIVE = torch.ops.aten.linalg_matrix_exp.default
 _DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 _ROUTED = (torch.linalg.matrix_exp, torch.matrix_exp, torch.Tensor.matrix_exp)
 _MAX_N = 32
+_MIX_MAX_N = 4
 
 
 def _eligible(input: torch.Tensor) -> bool:
@@ -168,6 +169,60 @@ def matrix_exp_and_grad(input: torch.Tensor, grad_output: torch.Tensor) -> tuple
     return y.detach(), grad
 
 
+@torch.library.register_fake("flash_hypercons::_mix_streams")
+def _mix_streams_fake(h, streams):
+    torch._check(h.device.type == "cuda" and streams.device == h.device)
+    torch._check(h.ndim == 3 and streams.ndim == 3)
+    torch._check(h.shape[-1] == h.shape[-2])
+    torch._check(1 < h.shape[-1] <= _MIX_MAX_N)
+    torch._check(streams.shape[0] == h.shape[0] and streams.shape[1] == h.shape[1])
+    torch._check(h.dtype in _DTYPES and streams.dtype in _DTYPES)
+    return streams.new_empty(streams.shape)
+
+
+@torch.library.register_fake("flash_hypercons::_mix_streams_backward")
+def _mix_streams_backward_fake(h, streams, grad):
+    _mix_streams_fake(h, streams)
+    torch._check(grad.shape == streams.shape and grad.dtype == streams.dtype)
+    return streams.new_empty(streams.shape), h.new_empty(h.shape)
+
+
+def _mix_eligible(h, streams) -> bool:
+    if not (isinstance(h, torch.Tensor) and isinstance(streams, torch.Tensor)):
+        return False
+    if any(type(t) not in (torch.Tensor, torch.nn.Parameter) for t in (h, streams)):
+        return False
+    if torch._C._are_functorch_transforms_active() or _has_tangent(h) or _has_tangent(streams):
+        return False
+    if h.device.type != "cuda" or torch.version.hip is not None or streams.device != h.device:
+        return False
+    if h.layout != torch.strided or streams.layout != torch.strided or h.ndim != 3 or streams.ndim != 3:
+        return False
+    n = h.shape[-1]
+    return (h.shape[-2] == n and 1 < n <= _MIX_MAX_N and tuple(streams.shape[:2]) == tuple(h.shape[:2])
+            and h.dtype in _DTYPES and streams.dtype in _DTYPES)
+
+
+def mix_streams(h: torch.Tensor, streams: torch.Tensor) -> torch.Tensor:
+    """Hyper-connection stream mixing with an exponential mixing matrix: ``exp(h) @ streams``.
+
+    ``h`` is ``[T, n, n]`` (one mixing generator per token, 2 <= n <= 4) and ``streams`` is
+    ``[T, n, D]`` (the token's n residual streams).  On CUDA, float32 / float16 / bfloat16, one
+    kernel computes exp(h[t]) in registers and applies it to the streams -- the exponential is
+    never written to memory -- and the backward is one kernel as well (d streams =
+    exp(h)^T dY, d h = the Frechet backward of exp at h for dY streams^T).  The result has the
+    streams' dtype; math is float32.  Other inputs, forward AD, function transforms and tensor
+    subclasses use native PyTorch (half types computed in float32).
+    (Extension of this package: the reference computes exp only.)
+    """
+    if _mix_eligible(h, streams):
+        return torch.ops.flash_hypercons._mix_streams(h, streams)
+    dt = torch.promote_types(h.dtype, streams.dtype)
+    if dt in (torch.float16, torch.bfloat16):
+        dt = torch.float32
+    return (torch.linalg.matrix_exp(h.to(dt)) @ streams.to(dt)).to(streams.dtype)
+
+
 class _MatrixExpMode(TorchFunctionMode):
     """Routes the three Python matrix-exp entry points to ``matrix_exp`` when called with a
     single tensor (positionally or as ``input=``); everything else passes through unchanged
@@ -193,4 +248,4 @@ def use_backend() -> TorchFunctionMode:
     return _MatrixExpMode()
 
 
-__all__ = ["matrix_exp", "matrix_exp_and_grad", "use_backend"]
+__all__ = ["matrix_exp", "matrix_exp_and_grad", "mix_streams", "use_backend"]

@@ -8,7 +8,7 @@ package's module paths resolve to the same module objects: ``flash_hypercons.ops
 
 import sys as _sys
 
-from flash_hyperconnections_b200 import __version__, _C, matrix_exp, matrix_exp_and_grad, ops, use_backend  # noqa: F401
+from flash_hyperconnections_b200 import __version__, _C, matrix_exp, matrix_exp_and_grad, mix_streams, ops, use_backend  # noqa: F401
 from flash_hyperconnections_b200.ops import matrix_exp as _matrix_exp_module
 
 _sys.modules[__name__ + "._C"] = _C
