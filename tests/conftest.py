@@ -30,3 +30,20 @@ def pytest_collection_modifyitems(items):
 def seed():
     # Same seed as the reference test-suite (tests/conftest.py:13-15 of flash_hypercons).
     torch.manual_seed(9041)
+
+
+def count_fhx_launches(fn) -> int:
+    """Kernels of this package (``fhx::`` device code) that ``fn()`` launches, counted by the
+    CUDA profiler.  Where the profiler records no device activity at all for the launches
+    (CUPTI can drop kernel records after earlier profiling sessions in the same process), the
+    runtime launch calls recorded on the host side are counted instead."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    events = prof.key_averages()
+    device = [ev for ev in events if str(getattr(ev, "device_type", "")).endswith("CUDA")]
+    if device:
+        return sum(int(ev.count) for ev in device if "fhx::" in ev.key)
+    return sum(int(ev.count) for ev in events if ev.key in ("cudaLaunchKernel", "cudaLaunchKernelExC", "cuLaunchKernel"))

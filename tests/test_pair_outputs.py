@@ -8,12 +8,12 @@ import ctypes
 
 import pytest
 import torch
-from torch.profiler import ProfilerActivity, profile
 
 import flash_hypercons as fh
 from flash_hyperconnections_b200 import _native
 from oracle import expm_oracle as O
 
+from .conftest import count_fhx_launches
 from .test_routing import op_names
 
 DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
@@ -100,11 +100,7 @@ def test_forward_ad_runs_one_frechet_launch(dtype, n):
     assert O.per_matrix_error(tangent, O.frechet_fp64(a, e)).max() <= O.tolerance(_kind(dtype), True)
     with torch.autograd.forward_ad.dual_level():
         dual = torch.autograd.forward_ad.make_dual(a, e)
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fh.matrix_exp(dual)
-            torch.cuda.synchronize()
-    launches = sum(int(ev.count) for ev in prof.key_averages() if "fhx::" in ev.key)
-    assert launches == 1, [ev.key for ev in prof.key_averages()]
+        assert count_fhx_launches(lambda: fh.matrix_exp(dual)) == 1
 
 
 @pytest.mark.gpu
@@ -136,10 +132,7 @@ def test_matrix_exp_and_grad_matches_autograd(dtype, n):
     assert torch.equal(grad, grad_ref)  # same Frechet kernel on the same view a.mT
     assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance(_kind(dtype), False)
     assert O.per_matrix_error(grad, O.frechet_fp64(a.mT, g)).max() <= O.tolerance(_kind(dtype), True)
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        fh.matrix_exp_and_grad(a, g)
-        torch.cuda.synchronize()
-    assert sum(int(ev.count) for ev in prof.key_averages() if "fhx::" in ev.key) == 1
+    assert count_fhx_launches(lambda: fh.matrix_exp_and_grad(a, g)) == 1
 
 
 def test_matrix_exp_and_grad_cpu_uses_native():

@@ -10,11 +10,12 @@ import ctypes
 
 import pytest
 import torch
-from torch.profiler import ProfilerActivity, profile
 
 import flash_hypercons as fh
 from flash_hyperconnections_b200 import _native
 from oracle import expm_oracle as O
+
+from .conftest import count_fhx_launches
 
 TOL = {torch.float32: 1e-5, torch.float16: 1e-2, torch.bfloat16: 1e-2}
 
@@ -125,12 +126,14 @@ def test_stream_mix_one_launch_each_way_and_deterministic():
     h, x, dy = _inputs(300, 4, 2048, torch.bfloat16, torch.bfloat16)
     hh = h.detach().requires_grad_()
     xx = x.detach().requires_grad_()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        y = fh.mix_streams(hh, xx)
-        grads = torch.autograd.grad(y, (xx, hh), dy)
-        torch.cuda.synchronize()
-    kernels = [ev.key for ev in prof.key_averages() if "fhx::" in ev.key]
-    assert sum(int(ev.count) for ev in prof.key_averages() if "fhx::" in ev.key) == 2, kernels
+    out = {}
+
+    def step():
+        out["y"] = fh.mix_streams(hh, xx)
+        out["grads"] = torch.autograd.grad(out["y"], (xx, hh), dy)
+
+    assert count_fhx_launches(step) == 2
+    y, grads = out["y"], out["grads"]
     y2 = fh.mix_streams(hh, xx)
     grads2 = torch.autograd.grad(y2, (xx, hh), dy)
     assert torch.equal(y, y2) and all(torch.equal(a, b) for a, b in zip(grads, grads2))
