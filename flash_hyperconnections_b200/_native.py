@@ -37,7 +37,15 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_matrix_exp.restype = i32
     lib.fhx_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i64, i32, i32, vp]
     lib.fhx_frechet.restype = i32
-    lib.fhx_matrix_exp_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i32, vp, i64, i32, i32, vp]
+    sz = ctypes.c_size_t
+    lib.fhx_workspace_bytes.argtypes = [i64, i32]
+    lib.fhx_workspace_bytes.restype = sz
+    lib.fhx_matrix_exp_ws.argtypes = [vp, i64, i64, i64, i32, vp, i64, i32, i32, vp, sz, vp]
+    lib.fhx_matrix_exp_ws.restype = i32
+    lib.fhx_frechet_ws.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i64, i32, i32, vp, sz, vp]
+    lib.fhx_frechet_ws.restype = i32
+    lib.fhx_matrix_exp_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i32, vp, i64, i32, i32,
+                                           vp, sz, vp]
     lib.fhx_matrix_exp_frechet.restype = i32
     lib.fhx_stream_mix.argtypes = [vp, i64, i64, i64, i32, i32, vp, i64, i64, i32, vp, i64, i32, i64, vp]
     lib.fhx_stream_mix.restype = i32

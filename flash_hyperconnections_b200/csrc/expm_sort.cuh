@@ -1,0 +1,210 @@
+// Degree classification and grouping for the team kernels whose teams share a warp (5 <= n <= 16).
+//
+// Teams in one warp run in lockstep, so a warp costs as much as its most expensive matrix.  On a
+// batch of mixed norms (config 3: degrees 4/8/12/18 in about equal shares, 0-4 squarings) that
+// is 7.4 product steps per 8 x 8 matrix where the matrices themselves need 4.0.  Before the main
+// kernel, three small passes group the batch by cost:
+//
+//   classify   one thread per matrix: nu = min(||A||_1, ||A||_inf) in float64 (rows and columns
+//              each summed in ascending order, so A and A^T give the same bits), (m, s) by
+//              choose_degree, a 16-bit key per matrix, and a histogram of key bins;
+//   scan       exclusive prefix sum of the histogram (one CTA);
+//   scatter    every matrix's index into its bin's range of a permutation.
+//
+// The main kernel then takes its matrices in permutation order and each team runs its matrix's
+// own (m, s) from the key: a matrix's result depends on that matrix alone (no degree shared with
+// neighbours), and the Frechet backward on A^T repeats the forward's (m, s) exactly.  The order
+// inside a bin (from shared-memory atomics) varies from run to run; it only decides which team
+// computes which matrix, never a result.
+//
+// Workspace (caller-allocated, fhx_workspace_bytes): keys (2 B per matrix), permutation (4 B per
+// matrix), histogram and bin cursors (kSortBins words each).
+#pragma once
+
+#include "expm_common.cuh"
+
+namespace fhx {
+
+constexpr int kSortThreads = 256;
+constexpr int kKeySMax = 31;                       // squarings beyond this share one bin
+constexpr int kSortBins = 6 * (kKeySMax + 1) + 1;  // (degree, s) bins + one for non-finite
+constexpr unsigned short kKeyBad = 0xffffu;        // a non-finite entry
+
+__host__ __device__ __forceinline__ int degree_index(int m) {
+  return m == 1 ? 0 : m == 2 ? 1 : m == 4 ? 2 : m == 8 ? 3 : m == 12 ? 4 : 5;
+}
+__host__ __device__ __forceinline__ int degree_of_index(int i) {
+  return i == 0 ? 1 : i == 1 ? 2 : i == 2 ? 4 : i == 3 ? 8 : i == 4 ? 12 : 18;
+}
+// key: bits 0-2 degree index, bits 3-15 squarings (s <= 8191 covers every float32 input)
+__host__ __device__ __forceinline__ unsigned short make_key(int m, int s) {
+  return static_cast<unsigned short>(degree_index(m) | (s << 3));
+}
+__device__ __forceinline__ int key_bin(unsigned short key) {
+  if (key == kKeyBad) return kSortBins - 1;
+  const int s = key >> 3;
+  return (key & 7) * (kKeySMax + 1) + (s < kKeySMax ? s : kKeySMax);
+}
+
+struct SortWorkspace {
+  unsigned short* keys;
+  int* perm;
+  unsigned* hist;
+  unsigned* cursor;
+};
+
+__host__ __forceinline__ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+__host__ __forceinline__ size_t sort_workspace_bytes(int64_t batch) {
+  return align256(size_t(batch) * 2) + align256(size_t(batch) * 4) + 2 * align256(kSortBins * 4);
+}
+
+__host__ __forceinline__ SortWorkspace sort_workspace(void* base, int64_t batch) {
+  char* p = static_cast<char*>(base);
+  SortWorkspace w;
+  w.keys = reinterpret_cast<unsigned short*>(p);
+  p += align256(size_t(batch) * 2);
+  w.perm = reinterpret_cast<int*>(p);
+  p += align256(size_t(batch) * 4);
+  w.hist = reinterpret_cast<unsigned*>(p);
+  p += align256(kSortBins * 4);
+  w.cursor = reinterpret_cast<unsigned*>(p);
+  return w;
+}
+
+// Block-level histogram of the bins in `bin` (-1: no matrix), added to the global one.
+__device__ __forceinline__ void add_block_histogram(int bin, unsigned* __restrict__ hist, unsigned* s_cnt) {
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  if (bin >= 0) atomicAdd(&s_cnt[bin], 1u);
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x)
+    if (s_cnt[i]) atomicAdd(&hist[i], s_cnt[i]);
+}
+
+// Four consecutive elements of a matrix along its contiguous dimension, as floats.
+__device__ __forceinline__ float4 load_vec4(const View& v, int dtype, int64_t off) {
+  if (dtype == kF32) return ld_f32x4(static_cast<const float*>(v.data) + off);
+  const uint2 h = ld_u32x2(reinterpret_cast<const unsigned*>(static_cast<const unsigned short*>(v.data) + off));
+  auto dec = [&](unsigned w) {
+    const unsigned short u = static_cast<unsigned short>(w);
+    return dtype == kBF16 ? __bfloat162float(__ushort_as_bfloat16(u)) : __half2float(__ushort_as_half(u));
+  };
+  return make_float4(dec(h.x & 0xffffu), dec(h.x >> 16), dec(h.y & 0xffffu), dec(h.y >> 16));
+}
+
+// Classification flags: bit 0 = rows are the contiguous dimension (else columns), bit 1 = the
+// contiguous dimension moves in aligned 4-element vectors (n % 4 == 0).
+enum : unsigned { kClsRows = 1u, kClsVec = 2u };
+
+// One thread per matrix of a strided [batch, n, n] view (P = 8 or 16 bounds n).  Row sums
+// accumulate over ascending columns and column sums over ascending rows whatever the loop
+// order, so the float64 norms of A and A^T are bit-identical.
+template <int P>
+__global__ void __launch_bounds__(kSortThreads) classify_kernel(View a, int64_t batch, int n, int dtype,
+                                                                unsigned flags, SortWorkspace ws) {
+  __shared__ unsigned s_cnt[kSortBins];
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  int bin = -1;
+  if (b < batch) {
+    double row[P], col[P];
+#pragma unroll
+    for (int t = 0; t < P; ++t) row[t] = col[t] = 0.0;
+    bool bad = false;
+    const int64_t base = b * a.s0;
+    const bool rows = flags & kClsRows;
+    auto add = [&](int i, int j, float v) {
+      bad |= !isfinite(v);
+      const double av = fabs(double(v));
+      row[i] += av;
+      col[j] += av;
+    };
+    if (flags & kClsVec) {
+      // along the contiguous dimension in 4-element vectors (n % 4 == 0)
+#pragma unroll
+      for (int o = 0; o < P; ++o) {
+#pragma unroll
+        for (int q = 0; q < P; q += 4) {
+          if (o < n && q < n) {
+            const int64_t off = rows ? base + o * a.s1 + q * a.s2 : base + q * a.s1 + o * a.s2;
+            const float4 x = load_vec4(a, dtype, off);
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (rows) add(o, q + u, xs[u]);
+              else add(q + u, o, xs[u]);
+            }
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int o = 0; o < P; ++o)
+#pragma unroll
+        for (int q = 0; q < P; ++q)
+          if (o < n && q < n) {
+            // (the sign of a negated view does not change |a|)
+            if (rows) add(o, q, load_elem(a.data, dtype, base + o * a.s1 + q * a.s2));
+            else add(q, o, load_elem(a.data, dtype, base + q * a.s1 + o * a.s2));
+          }
+    }
+    double nrow = 0.0, ncol = 0.0;
+#pragma unroll
+    for (int t = 0; t < P; ++t) {
+      nrow = fmax(nrow, row[t]);
+      ncol = fmax(ncol, col[t]);
+    }
+    unsigned short key = kKeyBad;
+    if (!bad) {
+      int m, s;
+      choose_degree(fmin(nrow, ncol), &m, &s);
+      key = make_key(m, s);
+    }
+    ws.keys[b] = key;
+    bin = key_bin(key);
+  }
+  add_block_histogram(bin, ws.hist, s_cnt);
+}
+
+// Exclusive prefix sum of the histogram into hist (bin starts); cursors to zero.  One CTA.
+__global__ void __launch_bounds__(kSortThreads) scan_bins_kernel(SortWorkspace ws) {
+  __shared__ unsigned s_v[kSortBins];
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) {
+    s_v[i] = ws.hist[i];
+    ws.cursor[i] = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned run = 0;
+    for (int i = 0; i < kSortBins; ++i) {
+      const unsigned c = s_v[i];
+      s_v[i] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) ws.hist[i] = s_v[i];
+}
+
+// perm[start(bin) + rank] = b: a CTA reserves one range per bin with a global atomic and hands
+// out ranks inside it with shared-memory atomics.
+__global__ void __launch_bounds__(kSortThreads) scatter_kernel(int64_t batch, SortWorkspace ws) {
+  __shared__ unsigned s_cnt[kSortBins];
+  __shared__ unsigned s_base[kSortBins];
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  int bin = -1;
+  unsigned local = 0;
+  if (b < batch) {
+    bin = key_bin(ws.keys[b]);
+    local = atomicAdd(&s_cnt[bin], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x)
+    if (s_cnt[i]) s_base[i] = ws.hist[i] + atomicAdd(&ws.cursor[i], s_cnt[i]);
+  __syncthreads();
+  if (bin >= 0) ws.perm[s_base[bin] + local] = int(b);
+}
+
+}  // namespace fhx

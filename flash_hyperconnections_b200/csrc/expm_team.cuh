@@ -37,6 +37,7 @@
 #pragma once
 
 #include "expm_common.cuh"
+#include "expm_sort.cuh"
 
 namespace fhx {
 
@@ -596,12 +597,23 @@ __device__ __forceinline__ void store_plane(const float* __restrict__ res, void*
   }
 }
 
+__device__ __forceinline__ int ld_s32(const int* p) {
+  int v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // out: the result (exp(A), or L(A, E) for Frechet launches); out2 (Frechet launches only,
 // may be null): exp(A) of the same launch -- the value part of the pair -- transposed when
 // flags has kOut2T.
+// perm, keys (both null, or both set): grouped mode (expm_sort.cuh).  The team's k-th matrix is
+// perm[k] instead of k, and its (m, s) comes from keys[perm[k]] instead of the in-kernel norms;
+// no degree is shared between teams.
 template <int P, int TM, int TN, bool Pair, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
-                                                                  void* __restrict__ out2, int64_t batch, int n, int dtype, unsigned flags) {
+                                                                  void* __restrict__ out2, const int* __restrict__ perm,
+                                                                  const unsigned short* __restrict__ keys,
+                                                                  int64_t batch, int n, int dtype, unsigned flags) {
   const bool a_rows = flags & kARows, a_vec = flags & kAVec;
   const bool e_rows = flags & kERows, e_vec = flags & kEVec;
   const bool out_vec = flags & kOutVec;
@@ -633,9 +645,17 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   constexpr int CHUNKS = P * P / 4;
   constexpr int PER_THREAD = (CHUNKS * C::NPART + T - 1) / T;
   uint4 vals[PER_THREAD];
+  int64_t pf_b = 0;     // matrix index of the prefetched matrix
+  unsigned pf_key = 0;  // and its key (grouped mode)
+  const bool grouped = perm != nullptr;
   auto fetch = [&](int64_t next_item) {
-    const int64_t nb = next_item * TPC + tic;
+    int64_t nb = next_item * TPC + tic;
     const bool ok = nb < batch;
+    if (grouped && ok) {
+      nb = ld_s32(perm + nb);
+      pf_key = ld_u16(keys + nb);
+    }
+    pf_b = nb;
 #pragma unroll
     for (int k = 0; k < PER_THREAD; ++k) {
       const int idx = t + k * T;
@@ -653,8 +673,9 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   };
   fetch(blockIdx.x);
   for (int64_t item = blockIdx.x; item * TPC < batch; item += gridDim.x) {
-    const int64_t b = item * TPC + tic;
-    const bool valid = b < batch;
+    const bool valid = item * TPC + tic < batch;
+    const int64_t b = pf_b;
+    const unsigned key = pf_key;
 
     // ---- A (and E) of this matrix, prefetched during the previous one, into slot 0 ----
     bool bad = false;
@@ -683,80 +704,87 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     fetch(item + gridDim.x);  // next matrix of this team: loads stay in flight during the steps
     if (bad) scratch[3] = 1;
     team_sync<T>(tic);
-    // ---- norms: sums of |row| and |column| of A, maxima over the team ----
-    // Sums of |a| in four float32 partial sums combined in float64; a partial sum that
-    // overflows float32 (entries near the float32 limit) is redone in float64.  Multi-warp
-    // teams split the work: threads 0..P-1 rows, P..2P-1 columns.
-    auto line_sum = [&](int l, bool column) {
-      // element k of line l: a[l][k] for a row, a[k][l] for a column
-      auto at = [&](int k) { return team[column ? pidx<P, TM>(k, l) : pidx<P, TM>(l, k)]; };
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int k = 0; k < P; ++k) ps[k & 3] += fabsf(at(k));
-      double sum = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
-      if (!isfinite(sum)) {
-        sum = 0.0;
-#pragma unroll 1
-        for (int k = 0; k < P; ++k) sum += fabs(double(at(k)));
+    int m = 1, s = 0, nsteps = 0;
+    if (grouped) {
+      if (key != kKeyBad) {
+        m = degree_of_index(int(key & 7u));
+        s = int(key >> 3);
       }
-      return sum;
-    };
-    static_assert(T <= 32 || (P == 32 && T >= 2 * P), "team norm split");
-    double nrow = 0.0, ncol = 0.0;
-    if constexpr (T > 32) {
-      if (t < P) {
-        // row t with 128-bit loads; same partial sums (element k into ps[k % 4], k ascending)
+    } else {
+      // ---- norms: sums of |row| and |column| of A, maxima over the team ----
+      // Sums of |a| in four float32 partial sums combined in float64; a partial sum that
+      // overflows float32 (entries near the float32 limit) is redone in float64.  Multi-warp
+      // teams split the work: threads 0..P-1 rows, P..2P-1 columns.
+      auto line_sum = [&](int l, bool column) {
+        // element k of line l: a[l][k] for a row, a[k][l] for a column
+        auto at = [&](int k) { return team[column ? pidx<P, TM>(k, l) : pidx<P, TM>(l, k)]; };
         float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c4 = 0; c4 < P / 4; ++c4) {
-          const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(t, 4 * c4));
-          ps[0] += fabsf(x.x);
-          ps[1] += fabsf(x.y);
-          ps[2] += fabsf(x.z);
-          ps[3] += fabsf(x.w);
+        for (int k = 0; k < P; ++k) ps[k & 3] += fabsf(at(k));
+        double sum = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
+        if (!isfinite(sum)) {
+          sum = 0.0;
+#pragma unroll 1
+          for (int k = 0; k < P; ++k) sum += fabs(double(at(k)));
         }
-        nrow = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
-        if (!isfinite(nrow)) nrow = line_sum(t, false);
-      } else if (t < 2 * P) {
-        ncol = line_sum(t - P, true);
-      }
-    } else {
-      for (int l = t; l < P; l += T) {
-        nrow = fmax(nrow, line_sum(l, false));
-        ncol = fmax(ncol, line_sum(l, true));
-      }
-    }
-    int m = 1, s = 0, nsteps = 0;
-    if constexpr (T <= 32) {
-      // Max over all T lanes of the team: every lane must end with the team's (m, s).  Lanes
-      // t >= P (teams wider than the matrix) hold no line and contribute 0.
+        return sum;
+      };
+      static_assert(T <= 32 || (P == 32 && T >= 2 * P), "team norm split");
+      double nrow = 0.0, ncol = 0.0;
+      if constexpr (T > 32) {
+        if (t < P) {
+          // row t with 128-bit loads; same partial sums (element k into ps[k % 4], k ascending)
+          float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int off = 1; off < T; off <<= 1) {
-        nrow = fmax(nrow, __shfl_xor_sync(0xffffffffu, nrow, off));
-        ncol = fmax(ncol, __shfl_xor_sync(0xffffffffu, ncol, off));
+          for (int c4 = 0; c4 < P / 4; ++c4) {
+            const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(t, 4 * c4));
+            ps[0] += fabsf(x.x);
+            ps[1] += fabsf(x.y);
+            ps[2] += fabsf(x.z);
+            ps[3] += fabsf(x.w);
+          }
+          nrow = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
+          if (!isfinite(nrow)) nrow = line_sum(t, false);
+        } else if (t < 2 * P) {
+          ncol = line_sum(t - P, true);
+        }
+      } else {
+        for (int l = t; l < P; l += T) {
+          nrow = fmax(nrow, line_sum(l, false));
+          ncol = fmax(ncol, line_sum(l, true));
+        }
       }
-    } else {
-      // warp 0 holds the row sums, warp 1 the column sums (P = 32)
-      double* maxima = reinterpret_cast<double*>(scratch + 4);
-      if (t < 64) {
-        double v = t < 32 ? nrow : ncol;
+      if constexpr (T <= 32) {
+        // Max over all T lanes of the team: every lane must end with the team's (m, s).  Lanes
+        // t >= P (teams wider than the matrix) hold no line and contribute 0.
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if ((t & 31) == 0) maxima[t >> 5] = v;
+        for (int off = 1; off < T; off <<= 1) {
+          nrow = fmax(nrow, __shfl_xor_sync(0xffffffffu, nrow, off));
+          ncol = fmax(ncol, __shfl_xor_sync(0xffffffffu, ncol, off));
+        }
+      } else {
+        // warp 0 holds the row sums, warp 1 the column sums (P = 32)
+        double* maxima = reinterpret_cast<double*>(scratch + 4);
+        if (t < 64) {
+          double v = t < 32 ? nrow : ncol;
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, off));
+          if ((t & 31) == 0) maxima[t >> 5] = v;
+        }
+        team_sync<T>(tic);  // also: every column read is done before tiles are rescaled
+        nrow = maxima[0];
+        ncol = maxima[1];
       }
-      team_sync<T>(tic);  // also: every column read is done before tiles are rescaled
-      nrow = maxima[0];
-      ncol = maxima[1];
-    }
-    choose_degree(fmin(nrow, ncol), &m, &s);
-    if constexpr (T < 32) {
-      // Teams that share a warp run one program, of the largest degree chosen in the warp:
-      // the step epilogues of different degrees would otherwise run one after another
-      // (measured: 30% of the 8 x 8 Frechet time on mixed-degree batches).  A team keeps its
-      // own s, which stays valid for a higher degree (theta_m grows with m), so accuracy never
-      // drops; the degree of a matrix then depends on the aligned group of 32 / T matrices
-      // that shares its warp.
-      m = int(__reduce_max_sync(0xffffffffu, unsigned(m)));
+      choose_degree(fmin(nrow, ncol), &m, &s);
+      if constexpr (T < 32) {
+        // Teams that share a warp run one program, of the largest degree chosen in the warp:
+        // the step epilogues of different degrees would otherwise run one after another
+        // (measured: 30% of the 8 x 8 Frechet time on mixed-degree batches).  A team keeps its
+        // own s, which stays valid for a higher degree (theta_m grows with m), so accuracy never
+        // drops; the degree of a matrix then depends on the aligned group of 32 / T matrices
+        // that shares its warp.
+        m = int(__reduce_max_sync(0xffffffffu, unsigned(m)));
+      }
     }
     {
       const bool bad_team = scratch[3] != 0;

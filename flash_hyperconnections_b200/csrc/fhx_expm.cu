@@ -131,7 +131,7 @@ unsigned layout_flags(const View& a, const View& e, const void* out, const void*
 // threads; one CTA holds WARPS * 32 / team-size teams.
 template <int P, int TM, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
-                cudaStream_t stream) {
+                cudaStream_t stream, const SortWorkspace* grouped = nullptr) {
   using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int threads = WARPS * 32;
   constexpr int teams = threads / C::T;
@@ -148,15 +148,45 @@ int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t
   const int64_t items = (batch + teams - 1) / teams;
   const int64_t resident = int64_t(sms) * per_sm;
   const int blocks = int(items < resident ? items : resident);
-  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, batch, n, dtype,
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, grouped ? grouped->perm : nullptr,
+                                            grouped ? grouped->keys : nullptr, batch, n, dtype,
                                             layout_flags<P>(a, e, out, out2, out2_t, n, dtype, Pair));
   return cuda_status(cudaGetLastError());
 }
 
+// Grouping passes of expm_sort.cuh on the view `a` (5 <= n <= 16): keys, histogram, bin starts,
+// permutation, in the caller's workspace.
+template <int P>
+int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* workspace, cudaStream_t stream,
+                    SortWorkspace* out) {
+  const SortWorkspace w = sort_workspace(workspace, batch);
+  int st = cuda_status(cudaMemsetAsync(w.hist, 0, kSortBins * sizeof(unsigned), stream));
+  if (st != FHX_OK) return st;
+  // the contiguous dimension of the view, and whether it moves in aligned 4-element vectors
+  const bool rows = a.s2 == 1 || (a.s1 != 1 && a.s2 <= a.s1);
+  const int64_t outer = rows ? a.s1 : a.s2;
+  const int64_t inner = rows ? a.s2 : a.s1;
+  unsigned flags = rows ? kClsRows : 0u;
+  if (n % 4 == 0 && inner == 1 && outer % 4 == 0 && a.s0 % 4 == 0 && aligned(a.data, dtype == kF32 ? 16 : 8))
+    flags |= kClsVec;
+  const int64_t blocks = (batch + kSortThreads - 1) / kSortThreads;
+  if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
+  classify_kernel<P><<<unsigned(blocks), kSortThreads, 0, stream>>>(a, batch, n, dtype, flags, w);
+  scan_bins_kernel<<<1, kSortThreads, 0, stream>>>(w);
+  scatter_kernel<<<unsigned(blocks), kSortThreads, 0, stream>>>(batch, w);
+  st = cuda_status(cudaGetLastError());
+  if (st != FHX_OK) return st;
+  *out = w;
+  return FHX_OK;
+}
+
+bool grouped_size(int n) { return n >= 5 && n <= 16; }
+
 // out2 (Frechet launches only, may be null): also write exp(A) there, transposed if out2_t.
+// workspace (may be null): for 5 <= n <= 16, group the batch by degree first (expm_sort.cuh).
 template <bool Pair>
 int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream,
-             void* out2 = nullptr, bool out2_t = false) {
+             void* out2 = nullptr, bool out2_t = false, void* workspace = nullptr) {
   switch (n) {
     case 2: return launch_reg<2, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
     case 3: return launch_reg<3, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
@@ -170,12 +200,20 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   // state per matrix).  8 x 8: 4 x 4 tiles, eight teams per warp.  16 x 16: forward 4 x 4 tiles,
   // two teams per warp; Frechet 2 x 4 tiles, one team per warp (20 % faster than 4 x 4 tiles,
   // whose 254 registers left 8 warps per SM).
-  if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+  SortWorkspace ws{};
+  const SortWorkspace* grouped = nullptr;
+  if (workspace != nullptr && grouped_size(n)) {
+    const int st = n <= 8 ? group_by_degree<8>(a, batch, n, dtype, workspace, stream, &ws)
+                          : group_by_degree<16>(a, batch, n, dtype, workspace, stream, &ws);
+    if (st != FHX_OK) return st;
+    grouped = &ws;
+  }
+  if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
   if (n <= 16) {
     if constexpr (Pair) {
-      return launch_team<16, 2, 4, true, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+      return launch_team<16, 2, 4, true, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
     } else {
-      return launch_team<16, 4, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+      return launch_team<16, 4, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
     }
   }
   if constexpr (Pair) {
@@ -240,10 +278,53 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
   return dispatch<true>(a, e, output, batch, n, dtype, static_cast<cudaStream_t>(stream));
 }
 
+size_t fhx_workspace_bytes(int64_t batch, int32_t n) {
+  if (batch <= 0 || !fhx::grouped_size(n)) return 0;
+  return fhx::sort_workspace_bytes(batch);
+}
+
+int32_t fhx_matrix_exp_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                          void* output, int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  if (workspace_bytes < fhx_workspace_bytes(batch, n) || (workspace == nullptr && workspace_bytes > 0))
+    return FHX_ERR_WORKSPACE;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View none{nullptr, 0, 0, 0, 1.f};
+  return dispatch<false>(a, none, output, batch, n, dtype, static_cast<cudaStream_t>(stream), nullptr, false,
+                         fhx_workspace_bytes(batch, n) ? workspace : nullptr);
+}
+
+int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                       const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
+                       void* output, int64_t batch, int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  st = check_view(direction, dir_s0, dir_s1, dir_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  if (workspace_bytes < fhx_workspace_bytes(batch, n) || (workspace == nullptr && workspace_bytes > 0))
+    return FHX_ERR_WORKSPACE;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View e{direction, dir_s0, dir_s1, dir_s2, dir_negate ? -1.f : 1.f};
+  return dispatch<true>(a, e, output, batch, n, dtype, static_cast<cudaStream_t>(stream), nullptr, false,
+                        fhx_workspace_bytes(batch, n) ? workspace : nullptr);
+}
+
 int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
                                const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
                                int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
-                               int64_t batch, int32_t n, int32_t dtype, void* stream) {
+                               int64_t batch, int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                               void* stream) {
   using namespace fhx;
   int st = check_common(batch, n, dtype, frechet_output);
   if (st != FHX_OK) return st;
@@ -253,10 +334,11 @@ int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, 
   st = check_view(direction, dir_s0, dir_s1, dir_s2, batch);
   if (st != FHX_OK) return st;
   if (batch == 0) return FHX_OK;
+  if (workspace != nullptr && workspace_bytes < fhx_workspace_bytes(batch, n)) return FHX_ERR_WORKSPACE;
   const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
   const View e{direction, dir_s0, dir_s1, dir_s2, dir_negate ? -1.f : 1.f};
   return dispatch<true>(a, e, frechet_output, batch, n, dtype, static_cast<cudaStream_t>(stream), exp_output,
-                        exp_transposed != 0);
+                        exp_transposed != 0, fhx_workspace_bytes(batch, n) ? workspace : nullptr);
 }
 
 const char* fhx_status_string(int32_t status) {
@@ -267,6 +349,7 @@ const char* fhx_status_string(int32_t status) {
     case FHX_ERR_POINTER: return "null data pointer for a non-empty batch";
     case FHX_ERR_STRIDE: return "negative stride";
     case FHX_ERR_CUDA: return "a CUDA runtime call or kernel launch failed (see fhx_last_cuda_error)";
+    case FHX_ERR_WORKSPACE: return "workspace smaller than fhx_workspace_bytes(batch, n)";
     default: return "unknown status";
   }
 }
@@ -275,6 +358,6 @@ int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda
 
 const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
 
-int32_t fhx_abi_version(void) { return 102; }
+int32_t fhx_abi_version(void) { return 103; }
 
 }  // extern "C"

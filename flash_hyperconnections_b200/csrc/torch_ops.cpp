@@ -54,6 +54,14 @@ void check_input(const at::Tensor& a) {
               "expected a strided CUDA [B, N, N] tensor, 2 <= N <= 32, in float32, float16, or bfloat16");
 }
 
+// Device workspace of the degree grouping (5 <= n <= 16), from the caching allocator; an
+// undefined tensor when the size needs none.
+at::Tensor workspace_for(const at::Tensor& a) {
+  const size_t bytes = fhx_workspace_bytes(a.size(0), static_cast<int32_t>(a.size(-1)));
+  if (bytes == 0) return at::Tensor();
+  return at::empty({static_cast<int64_t>(bytes)}, a.options().dtype(at::kByte));
+}
+
 at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
   check_input(a);
   if (direction != nullptr) {
@@ -67,15 +75,18 @@ at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
   void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
   const int64_t batch = a.size(0);
   const int32_t n = static_cast<int32_t>(a.size(-1));
+  const at::Tensor ws = workspace_for(a);
+  void* ws_ptr = ws.defined() ? ws.mutable_data_ptr() : nullptr;
+  const size_t ws_bytes = ws.defined() ? static_cast<size_t>(ws.numel()) : 0;
   int32_t status;
   if (direction == nullptr) {
-    status = fhx_matrix_exp(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
-                            out.mutable_data_ptr(), batch, n, dtype_code(a), stream);
+    status = fhx_matrix_exp_ws(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
+                               out.mutable_data_ptr(), batch, n, dtype_code(a), ws_ptr, ws_bytes, stream);
   } else {
     const at::Tensor& e = *direction;
-    status = fhx_frechet(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
-                         e.const_data_ptr(), e.stride(0), e.stride(1), e.stride(2), e.is_neg() ? 1 : 0,
-                         out.mutable_data_ptr(), batch, n, dtype_code(a), stream);
+    status = fhx_frechet_ws(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
+                            e.const_data_ptr(), e.stride(0), e.stride(1), e.stride(2), e.is_neg() ? 1 : 0,
+                            out.mutable_data_ptr(), batch, n, dtype_code(a), ws_ptr, ws_bytes, stream);
   }
   TORCH_CHECK(status == FHX_OK, "flash_hypercons kernel: ", fhx_status_string(status),
               status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
@@ -95,10 +106,12 @@ std::tuple<at::Tensor, at::Tensor> run_pair(const at::Tensor& a, const at::Tenso
   at::Tensor l = at::empty(a.sizes(), opts);
   if (a.numel() == 0) return {y, l};
   void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
+  const at::Tensor ws = workspace_for(a);
   const int32_t status = fhx_matrix_exp_frechet(
       a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0, e.const_data_ptr(), e.stride(0),
       e.stride(1), e.stride(2), e.is_neg() ? 1 : 0, y.mutable_data_ptr(), transposed ? 1 : 0, l.mutable_data_ptr(),
-      a.size(0), static_cast<int32_t>(a.size(-1)), dtype_code(a), stream);
+      a.size(0), static_cast<int32_t>(a.size(-1)), dtype_code(a), ws.defined() ? ws.mutable_data_ptr() : nullptr,
+      ws.defined() ? static_cast<size_t>(ws.numel()) : 0, stream);
   TORCH_CHECK(status == FHX_OK, "flash_hypercons kernel: ", fhx_status_string(status),
               status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
   return {y, l};

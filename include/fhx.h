@@ -21,6 +21,7 @@
 #ifndef FHX_H_
 #define FHX_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -40,6 +41,7 @@ extern "C" {
 #define FHX_ERR_STRIDE 4     /* negative stride                                         */
 #define FHX_ERR_CUDA 5       /* a CUDA runtime call or the kernel launch failed; the
                                 cudaError_t is kept for fhx_last_cuda_error()            */
+#define FHX_ERR_WORKSPACE 6  /* workspace smaller than fhx_workspace_bytes(batch, n)   */
 
 #define FHX_MAX_N 32
 #define FHX_MIX_MAX_N 4      /* streams per token of the fused stream mixing            */
@@ -62,12 +64,41 @@ int32_t fhx_matrix_exp(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
  * The number of squarings depends on A only and is identical for A and A^T.  The Taylor
  * degree does too, except where several matrices share a warp: for 5 <= n <= 8 (both entry
  * points) and for the forward at 9 <= n <= 16, a matrix runs the largest degree chosen in its
- * aligned group of 8 or 2 consecutive matrices, which is at least as accurate.
+ * aligned group of 8 or 2 consecutive matrices, which is at least as accurate; its output bits
+ * can then depend on those neighbours (within the tolerance).  Results are bit-stable for
+ * batch prefixes made of whole aligned groups and for re-runs of the same batch.
  * Any non-finite entry of A or E makes that matrix's whole output NaN.
  */
 int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
                     const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
                     void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
+
+/*
+ * Device workspace (bytes) that fhx_matrix_exp_ws / fhx_frechet_ws / fhx_matrix_exp_frechet need
+ * for a batch of n x n matrices: 6 bytes per matrix plus 2 KB for 5 <= n <= 16, 0 otherwise.
+ */
+size_t fhx_workspace_bytes(int64_t batch, int32_t n);
+
+/*
+ * fhx_matrix_exp and fhx_frechet with a caller-allocated device workspace of at least
+ * fhx_workspace_bytes(batch, n) bytes (16-byte aligned; contents on entry do not matter, and
+ * the workspace must not be used by another call in flight on the GPU at the same time).  For
+ * 5 <= n <= 16 the batch is first grouped by (degree, squarings) -- three small passes that
+ * classify every matrix in float64 and build a permutation -- so that the matrices that share a
+ * warp run the same program, and every matrix runs its own degree: its result depends on that
+ * matrix alone (bit-stable under any batching), and fhx_frechet_ws on A^T repeats the (m, s) of
+ * fhx_matrix_exp_ws on A exactly.  Other n ignore the workspace (workspace_bytes may be 0).
+ * Reference interfaces: as fhx_matrix_exp / fhx_frechet (the workspace replaces the
+ * reference's per-call pre-copies, csrc/matrix_exp.cu:35-44, which the caching allocator
+ * provides there).
+ */
+int32_t fhx_matrix_exp_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                          void* output, int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                          size_t workspace_bytes, void* stream);
+int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                       const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
+                       void* output, int64_t batch, int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                       void* stream);
 
 /*
  * exp(A) and L(A, E) from ONE launch: the Frechet kernel carries the pair (exp, derivative)
@@ -80,9 +111,11 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
  *   - forward and backward of Y = exp(X) together, when the upstream gradient G is known:
  *     pass A = X^T (in_s1/in_s2 swapped), E = G, exp_transposed = 1; then
  *     exp_output = exp(X) = Y and frechet_output = L(X^T, G) = dL/dX.
- * The pair's degree and scaling are those of fhx_frechet on the same A, so frechet_output
- * equals fhx_frechet's output bit for bit; exp_output can differ from fhx_matrix_exp's in
- * the last bits where the forward kernel shares a degree between neighbouring matrices.
+ * workspace (may be null, else at least fhx_workspace_bytes(batch, n) bytes): as in
+ * fhx_frechet_ws.  The pair's degree and scaling are those of fhx_frechet (with a workspace:
+ * fhx_frechet_ws) on the same A, so frechet_output equals that call's output bit for bit;
+ * without a workspace, exp_output can differ from fhx_matrix_exp's in the last bits where the
+ * forward kernel shares a degree between neighbouring matrices.
  * Reference counterpart: none as one call.  It fuses the forward-AD rule of the reference
  * (native, flash_hypercons/ops/matrix_exp/__init__.py:89-94) and the forward + backward pair
  * _matrix_exp / _frechet (csrc/register.cpp:11-12) into one launch.
@@ -90,7 +123,8 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
 int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
                                const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
                                int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
-                               int64_t batch, int32_t n, int32_t dtype, void* stream);
+                               int64_t batch, int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /*
  * Hyper-connection stream mixing fused with the exponential, one warp per token:

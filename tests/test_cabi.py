@@ -18,12 +18,13 @@ DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 def declared_functions():
     text = HEADER.read_text()
-    return re.findall(r"^\s*(?:int32_t|const char\*)\s+(fhx_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^\s*(?:int32_t|size_t|const char\*)\s+(fhx_\w+)\s*\(", text, flags=re.M)
 
 
 def test_header_declares_entry_points():
     names = declared_functions()
-    for required in ("fhx_matrix_exp", "fhx_frechet", "fhx_status_string", "fhx_abi_version"):
+    for required in ("fhx_matrix_exp", "fhx_frechet", "fhx_status_string", "fhx_abi_version", "fhx_workspace_bytes",
+                     "fhx_matrix_exp_ws", "fhx_frechet_ws"):
         assert required in names
 
 
@@ -31,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_cabi()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.fhx_abi_version() == 102
+    assert lib.fhx_abi_version() == 103
 
 
 def test_status_strings():
@@ -65,6 +66,21 @@ def test_null_pointer_and_stride_errors_without_gpu():
     assert lib.fhx_frechet(buf, 16, 4, 1, 0, None, 16, 4, 1, 0, buf, 4, 4, 0, None) == 3
     # An empty batch is a no-op even with null pointers.
     assert lib.fhx_matrix_exp(None, 0, 0, 0, 0, None, 0, 4, 0, None) == 0
+
+
+def test_workspace_sizes_and_errors_without_gpu():
+    lib = _native.load_cabi()
+    # 6 bytes per matrix (key + permutation entry) plus the bin tables, for 5 <= n <= 16 only
+    assert lib.fhx_workspace_bytes(1000, 8) >= 6000
+    assert lib.fhx_workspace_bytes(1000, 16) == lib.fhx_workspace_bytes(1000, 5)
+    assert lib.fhx_workspace_bytes(1000, 4) == 0 and lib.fhx_workspace_bytes(1000, 17) == 0
+    assert lib.fhx_workspace_bytes(0, 8) == 0
+    buf = ctypes.c_void_p(256)
+    need = lib.fhx_workspace_bytes(64, 8)
+    # too small a workspace is rejected before any CUDA call
+    assert lib.fhx_matrix_exp_ws(buf, 64, 8, 1, 0, buf, 64, 8, 0, buf, need - 1, None) == 6
+    assert lib.fhx_frechet_ws(buf, 64, 8, 1, 0, buf, 64, 8, 1, 0, buf, 64, 8, 0, None, 0, None) == 6
+    assert b"workspace" in lib.fhx_status_string(6)
 
 
 def _call(lib, a, out, e=None, stream=None):

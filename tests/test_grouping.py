@@ -1,0 +1,101 @@
+"""Degree grouping of the team kernels for 5 <= n <= 16 (workspace entry points).
+
+With a workspace the batch is grouped by (degree, squarings) before the main kernel and every
+matrix runs its own degree, so a matrix's result depends on that matrix alone: its output bits
+must not change when its neighbours in the batch change.  Checked through ``fh.matrix_exp`` and
+its backward (which use the workspace entry points) on mixed-norm batches, plus the C ABI with
+and without a workspace against the float64 oracle (reference criterion per matrix)."""
+
+import pytest
+import torch
+
+import flash_hypercons as fh
+from flash_hyperconnections_b200 import _native
+from oracle import expm_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _mixed(batch, n, dtype, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    a = torch.randn(batch, n, n, generator=g) / n**0.5
+    a = a * torch.pow(10.0, torch.rand(batch, 1, 1, generator=g) * 4 - 3)  # every degree, 0-4 squarings
+    return a.to(dtype).cuda()
+
+
+def _fwd_bwd(a, g):
+    x = a.detach().requires_grad_()
+    y = fh.matrix_exp(x)
+    (grad,) = torch.autograd.grad(y, x, g)
+    return y.detach(), grad
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [5, 8, 12, 16])
+def test_result_independent_of_neighbours(n, dtype):
+    a = _mixed(1000, n, dtype, 7)
+    g = torch.randn(1000, n, n, dtype=torch.float32).to(dtype).cuda()
+    y, grad = _fwd_bwd(a, g)
+    # the same matrices in another order, and among other neighbours
+    perm = torch.randperm(1000)
+    y_p, grad_p = _fwd_bwd(a[perm], g[perm])
+    assert torch.equal(y_p, y[perm]) and torch.equal(grad_p, grad[perm])
+    other = _mixed(1000, n, dtype, 8)
+    mixed = torch.cat([other[:500], a[::2], other[500:]])
+    gm = torch.cat([g[:500], g[::2], g[500:]])
+    y_m, grad_m = _fwd_bwd(mixed, gm)
+    assert torch.equal(y_m[500:1000], y[::2]) and torch.equal(grad_m[500:1000], grad[::2])
+    kind = "float32" if dtype == torch.float32 else "half"
+    assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance(kind, False)
+    assert O.per_matrix_error(grad, O.frechet_fp64(a.mT, g)).max() <= O.tolerance(kind, True)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("n", [5, 8, 11, 16])
+@pytest.mark.parametrize("layout", ["contiguous", "transposed", "strided"])
+def test_cabi_workspace_paths(n, dtype, layout):
+    lib = _native.load_cabi()
+    batch = 300
+    base = _mixed(batch, n + 2, dtype, 3)
+    if layout == "contiguous":
+        a = base[:, :n, :n].contiguous()
+    elif layout == "transposed":
+        a = base[:, :n, :n].contiguous().mT
+    else:
+        a = base[:, 1:, 1:][:, :n, :n]
+    e = torch.randn(batch, n, n).to(dtype).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    nws = lib.fhx_workspace_bytes(batch, n)
+    ws = torch.full((nws,), 0xAB, dtype=torch.uint8, device="cuda")  # stale contents must not matter
+    kind = "float32" if dtype == torch.float32 else "half"
+    for grouped in (False, True):
+        y = torch.empty(batch, n, n, dtype=dtype, device="cuda")
+        l = torch.empty_like(y)
+        if grouped:
+            assert lib.fhx_matrix_exp_ws(a.data_ptr(), *a.stride(), 0, y.data_ptr(), batch, n, DT[dtype],
+                                         ws.data_ptr(), nws, stream) == 0
+            assert lib.fhx_frechet_ws(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, l.data_ptr(), batch,
+                                      n, DT[dtype], ws.data_ptr(), nws, stream) == 0
+        else:
+            assert lib.fhx_matrix_exp(a.data_ptr(), *a.stride(), 0, y.data_ptr(), batch, n, DT[dtype], stream) == 0
+            assert lib.fhx_frechet(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, l.data_ptr(), batch, n,
+                                   DT[dtype], stream) == 0
+        torch.cuda.synchronize()
+        assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance(kind, False)
+        assert O.per_matrix_error(l, O.frechet_fp64(a, e)).max() <= O.tolerance(kind, True)
+
+
+def test_grouped_nonfinite_and_degree_one():
+    a = _mixed(64, 8, torch.float32, 11)
+    a[3, 2, 2] = float("inf")
+    a[10] = 0.0  # degree 1: exp(0) = I
+    a[11] *= 1e-9
+    y = fh.matrix_exp(a)
+    assert y[3].isnan().all()
+    ok = torch.ones(64, dtype=torch.bool)
+    ok[3] = False
+    assert y[ok].isfinite().all()
+    assert torch.equal(y[10], torch.eye(8, device="cuda"))
+    assert O.per_matrix_error(y[ok], O.exp_fp64(a[ok])).max() <= O.tolerance("float32", False)

@@ -28,11 +28,13 @@ def test_pair_entry_point_rejects_bad_arguments_without_gpu():
     lib = _native.load_cabi()
     buf = ctypes.c_void_p(1)
     # n out of range, null exp output, null derivative output, negative stride
-    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, buf, 0, buf, 4, 33, 0, None) == 1
-    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, None, 0, buf, 4, 4, 0, None) == 3
-    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, buf, 0, None, 4, 4, 0, None) == 3
-    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, -16, 4, 1, 0, buf, 0, buf, 4, 4, 0, None) == 4
-    assert lib.fhx_matrix_exp_frechet(None, 0, 0, 0, 0, None, 0, 0, 0, 0, None, 0, None, 0, 4, 0, None) == 0
+    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, buf, 0, buf, 4, 33, 0, None, 0, None) == 1
+    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, None, 0, buf, 4, 4, 0, None, 0, None) == 3
+    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, 16, 4, 1, 0, buf, 0, None, 4, 4, 0, None, 0, None) == 3
+    assert lib.fhx_matrix_exp_frechet(buf, 16, 4, 1, 0, buf, -16, 4, 1, 0, buf, 0, buf, 4, 4, 0, None, 0, None) == 4
+    assert lib.fhx_matrix_exp_frechet(None, 0, 0, 0, 0, None, 0, 0, 0, 0, None, 0, None, 0, 4, 0, None, 0, None) == 0
+    # a workspace smaller than fhx_workspace_bytes is rejected
+    assert lib.fhx_matrix_exp_frechet(buf, 64, 8, 1, 0, buf, 64, 8, 1, 0, buf, 0, buf, 4, 8, 0, buf, 1, None) == 6
 
 
 @pytest.mark.gpu
@@ -50,13 +52,15 @@ def test_cabi_pair_outputs(dtype, n, transposed_view):
     e = (torch.randn(batch, n, n, device="cuda") * 0.5).to(dtype)
     stream = torch.cuda.current_stream().cuda_stream
     ref_l = torch.empty_like(e)
-    assert lib.fhx_frechet(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, ref_l.data_ptr(), batch, n,
-                           DT[dtype], stream) == 0
+    nws = lib.fhx_workspace_bytes(batch, n)
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device="cuda")
+    assert lib.fhx_frechet_ws(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, ref_l.data_ptr(), batch, n,
+                              DT[dtype], ws.data_ptr(), nws, stream) == 0
     for exp_t in (0, 1):
         y = torch.full_like(e, 7.0)
         l = torch.full_like(e, 7.0)
         assert lib.fhx_matrix_exp_frechet(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, y.data_ptr(),
-                                          exp_t, l.data_ptr(), batch, n, DT[dtype], stream) == 0
+                                          exp_t, l.data_ptr(), batch, n, DT[dtype], ws.data_ptr(), nws, stream) == 0
         torch.cuda.synchronize()
         assert torch.equal(l, ref_l)
         ref_y = O.exp_fp64(a)
@@ -76,7 +80,7 @@ def test_cabi_pair_outputs_nonfinite_rows():
         e[4, 1, 1] = float("inf")
         y, l = torch.empty_like(a), torch.empty_like(a)
         assert lib.fhx_matrix_exp_frechet(a.data_ptr(), *a.stride(), 0, e.data_ptr(), *e.stride(), 0, y.data_ptr(), 0,
-                                          l.data_ptr(), 6, n, 0, torch.cuda.current_stream().cuda_stream) == 0
+                                          l.data_ptr(), 6, n, 0, None, 0, torch.cuda.current_stream().cuda_stream) == 0
         torch.cuda.synchronize()
         for b in (1, 4):
             assert y[b].isnan().all() and l[b].isnan().all()
