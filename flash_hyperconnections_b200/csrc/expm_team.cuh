@@ -606,10 +606,10 @@ __device__ __forceinline__ int ld_s32(const int* p) {
 // out: the result (exp(A), or L(A, E) for Frechet launches); out2 (Frechet launches only,
 // may be null): exp(A) of the same launch -- the value part of the pair -- transposed when
 // flags has kOut2T.
-// perm, keys (both null, or both set): grouped mode (expm_sort.cuh).  The team's k-th matrix is
-// perm[k] instead of k, and its (m, s) comes from keys[perm[k]] instead of the in-kernel norms;
-// no degree is shared between teams.
-template <int P, int TM, int TN, bool Pair, int WARPS>
+// Grouped (perm, keys set; expm_sort.cuh): the team's k-th matrix is perm[k] instead of k, and
+// its (m, s) comes from keys[perm[k]] instead of the in-kernel norms; no degree is shared between
+// teams.  A template parameter, so that the ungrouped kernel carries none of it in registers.
+template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped>
 __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
                                                                   void* __restrict__ out2, const int* __restrict__ perm,
                                                                   const unsigned short* __restrict__ keys,
@@ -645,17 +645,19 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   constexpr int CHUNKS = P * P / 4;
   constexpr int PER_THREAD = (CHUNKS * C::NPART + T - 1) / T;
   uint4 vals[PER_THREAD];
-  int64_t pf_b = 0;     // matrix index of the prefetched matrix
-  unsigned pf_key = 0;  // and its key (grouped mode)
-  const bool grouped = perm != nullptr;
+  int64_t pf_b = 0;     // matrix index of the prefetched matrix (grouped mode)
+  unsigned pf_key = 0;  // and its key
+  constexpr bool grouped = Grouped;
   auto fetch = [&](int64_t next_item) {
     int64_t nb = next_item * TPC + tic;
     const bool ok = nb < batch;
-    if (grouped && ok) {
-      nb = ld_s32(perm + nb);
-      pf_key = ld_u16(keys + nb);
+    if constexpr (grouped) {
+      if (ok) {
+        nb = ld_s32(perm + nb);
+        pf_key = ld_u16(keys + nb);
+      }
+      pf_b = nb;
     }
-    pf_b = nb;
 #pragma unroll
     for (int k = 0; k < PER_THREAD; ++k) {
       const int idx = t + k * T;
@@ -674,7 +676,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   fetch(blockIdx.x);
   for (int64_t item = blockIdx.x; item * TPC < batch; item += gridDim.x) {
     const bool valid = item * TPC + tic < batch;
-    const int64_t b = pf_b;
+    const int64_t b = grouped ? pf_b : item * TPC + tic;
     const unsigned key = pf_key;
 
     // ---- A (and E) of this matrix, prefetched during the previous one, into slot 0 ----
@@ -705,7 +707,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     if (bad) scratch[3] = 1;
     team_sync<T>(tic);
     int m = 1, s = 0, nsteps = 0;
-    if (grouped) {
+    if constexpr (grouped) {
       if (key != kKeyBad) {
         m = degree_of_index(int(key & 7u));
         s = int(key >> 3);

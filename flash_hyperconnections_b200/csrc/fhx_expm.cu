@@ -129,15 +129,15 @@ unsigned layout_flags(const View& a, const View& e, const void* out, const void*
 
 // TM x TN: a thread's register tile; WARPS: warps per CTA.  A team is (P/TM) * (P/TN)
 // threads; one CTA holds WARPS * 32 / team-size teams.
-template <int P, int TM, int TN, bool Pair, int WARPS>
-int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
-                cudaStream_t stream, const SortWorkspace* grouped = nullptr) {
+template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped>
+int launch_team_kernel(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n,
+                       int dtype, cudaStream_t stream, const int* perm, const unsigned short* keys) {
   using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int threads = WARPS * 32;
   constexpr int teams = threads / C::T;
   constexpr size_t smem = size_t(teams) * C::TEAM_FLOATS * sizeof(float);
   static LaunchShape shape;
-  auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS>;
+  auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS, Grouped>;
   int dev = 0;
   const int st = cuda_status(cudaGetDevice(&dev));
   if (st != FHX_OK) return st;
@@ -148,10 +148,22 @@ int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t
   const int64_t items = (batch + teams - 1) / teams;
   const int64_t resident = int64_t(sms) * per_sm;
   const int blocks = int(items < resident ? items : resident);
-  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, grouped ? grouped->perm : nullptr,
-                                            grouped ? grouped->keys : nullptr, batch, n, dtype,
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, perm, keys, batch, n, dtype,
                                             layout_flags<P>(a, e, out, out2, out2_t, n, dtype, Pair));
   return cuda_status(cudaGetLastError());
+}
+
+// grouped (may be null): the permutation and keys of group_by_degree (P <= 16 only).
+template <int P, int TM, int TN, bool Pair, int WARPS>
+int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
+                cudaStream_t stream, const SortWorkspace* grouped = nullptr) {
+  if constexpr (P <= 16) {
+    if (grouped != nullptr)
+      return launch_team_kernel<P, TM, TN, Pair, WARPS, true>(a, e, out, out2, out2_t, batch, n, dtype, stream,
+                                                              grouped->perm, grouped->keys);
+  }
+  return launch_team_kernel<P, TM, TN, Pair, WARPS, false>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr,
+                                                           nullptr);
 }
 
 // Grouping passes of expm_sort.cuh on the view `a` (5 <= n <= 16): keys, histogram, bin starts,
