@@ -86,6 +86,14 @@ __device__ __forceinline__ void store_chunk(void* p, int dtype, int64_t off, flo
   }
 }
 
+// Index of degree m in (1, 2, 4, 8, 12, 18), and back.
+__host__ __device__ __forceinline__ int degree_index(int m) {
+  return m == 1 ? 0 : m == 2 ? 1 : m == 4 ? 2 : m == 8 ? 3 : m == 12 ? 4 : 5;
+}
+__host__ __device__ __forceinline__ int degree_of_index(int i) {
+  return i == 0 ? 1 : i == 1 ? 2 : i == 2 ? 4 : i == 3 ? 8 : i == 4 ? 12 : 18;
+}
+
 // Number of matrix products of the degree-m scheme (Bader-Blanes-Casas 2019).
 __host__ __device__ __forceinline__ int scheme_products(int m) {
   return m <= 1 ? 0 : m == 2 ? 1 : m == 4 ? 2 : m == 8 ? 3 : m == 12 ? 4 : 5;

@@ -116,64 +116,46 @@ __device__ __forceinline__ RMat<N, Pair> rcomb(const float (&c)[K + 1], const RM
   return r;
 }
 
-// Degree-m Taylor scheme of Bader-Blanes-Casas (2019) on an already scaled matrix.
+// The B1..B4 rows of every degree m <= 12 in the four-product structure of T12
+// (expm_coeffs.h, t12u), for lanes that index them at run time.
+struct T12UTable {
+  float v[5][4][4];
+};
+__host__ __device__ constexpr T12UTable make_t12u_table() {
+  T12UTable t{};
+  for (int d = 0; d < 5; ++d)
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) t.v[d][r][c] = t12u(d, r, c);
+  return t;
+}
+__constant__ T12UTable kT12U = make_t12u_table();
+
+// Degree-m Taylor scheme of Bader-Blanes-Casas (2019) on an already scaled matrix.  Every
+// degree m <= 12 runs one code path, the four-product structure of T12 (A2, A3, A6 = B4 B4 + B3,
+// T = (B2 + A6) A6 + B1) with its own coefficient rows: lanes of one warp whose matrices picked
+// different degrees then run one program instead of one branch per degree (on config 2's
+// degree-8/12 mix nearly every warp had both, 3 + 4 products).  Degree 18 has its own path.
 template <int N, bool Pair>
 __device__ __forceinline__ RMat<N, Pair> taylor(int m, const RMat<N, Pair>& a) {
   using M = RMat<N, Pair>;
-  if (m == 1) {
-    M r = rident<N, Pair>(1.f);
-    radd(r, a);
-    return r;
-  }
   const M a2 = rmul(a, a);
-  if (m == 2) {
-    M r = rident<N, Pair>(1.f);
-    radd(r, a);
-    raxpy(r, 0.5f, a2);
-    return r;
-  }
-  if (m == 4) {
-    M c = rident<N, Pair>(0.5f);
-    raxpy(c, 1.f / 6.f, a);
-    raxpy(c, 1.f / 24.f, a2);
-    M r = rmul(a2, c);
-    M f = rident<N, Pair>(1.f);
-    radd(f, a);
-    radd(r, f);
-    return r;
-  }
-  if (m == 8) {
-    M c1 = rident<N, Pair>(0.f);
-    raxpy(c1, kT8X1, a);
-    raxpy(c1, kT8X2, a2);
-    const M a4 = rmul(a2, c1);
-    M left = a4;
-    raxpy(left, kT8X3, a2);
-    M right = rident<N, Pair>(kT8X4);
-    raxpy(right, kT8X5, a);
-    raxpy(right, kT8X6, a2);
-    raxpy(right, kT8X7, a4);
-    M r = rmul(left, right);
-    M f = rident<N, Pair>(1.f);
-    radd(f, a);
-    raxpy(f, kT8Y2, a2);
-    radd(r, f);
-    return r;
-  }
   const M a3 = rmul(a2, a);
-  if (m == 12) {
-    const M* basis[3] = {&a, &a2, &a3};
-    const float c1[4] = {t12c(0, 0), t12c(0, 1), t12c(0, 2), t12c(0, 3)};
-    const float c2[4] = {t12c(1, 0), t12c(1, 1), t12c(1, 2), t12c(1, 3)};
-    const float c3[4] = {t12c(2, 0), t12c(2, 1), t12c(2, 2), t12c(2, 3)};
-    const float c4[4] = {t12c(3, 0), t12c(3, 1), t12c(3, 2), t12c(3, 3)};
-    const M b4 = rcomb<N, Pair, 3>(c4, basis);
+  if (m != 18) {
+    const float(&t)[4][4] = kT12U.v[degree_index(m)];
+    auto comb = [&](int r) {
+      M x = rident<N, Pair>(t[r][0]);
+      raxpy(x, t[r][1], a);
+      raxpy(x, t[r][2], a2);
+      raxpy(x, t[r][3], a3);
+      return x;
+    };
+    const M b4 = comb(3);
     M a6 = rmul(b4, b4);
-    radd(a6, rcomb<N, Pair, 3>(c3, basis));
-    M left = rcomb<N, Pair, 3>(c2, basis);
+    radd(a6, comb(2));
+    M left = comb(1);
     radd(left, a6);
     M r = rmul(left, a6);
-    radd(r, rcomb<N, Pair, 3>(c1, basis));
+    radd(r, comb(0));
     return r;
   }
   const M a6 = rmul(a3, a3);

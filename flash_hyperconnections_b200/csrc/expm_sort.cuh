@@ -1,4 +1,5 @@
-// Degree classification and grouping for the team kernels whose teams share a warp (5 <= n <= 16).
+// Degree classification and grouping for the team kernel whose teams share a warp (5 <= n <= 8:
+// eight 4-thread teams per warp).
 //
 // Teams in one warp run in lockstep, so a warp costs as much as its most expensive matrix.  On a
 // batch of mixed norms (config 3: degrees 4/8/12/18 in about equal shares, 0-4 squarings) that
@@ -30,12 +31,6 @@ constexpr int kKeySMax = 31;                       // squarings beyond this shar
 constexpr int kSortBins = 6 * (kKeySMax + 1) + 1;  // (degree, s) bins + one for non-finite
 constexpr unsigned short kKeyBad = 0xffffu;        // a non-finite entry
 
-__host__ __device__ __forceinline__ int degree_index(int m) {
-  return m == 1 ? 0 : m == 2 ? 1 : m == 4 ? 2 : m == 8 ? 3 : m == 12 ? 4 : 5;
-}
-__host__ __device__ __forceinline__ int degree_of_index(int i) {
-  return i == 0 ? 1 : i == 1 ? 2 : i == 2 ? 4 : i == 3 ? 8 : i == 4 ? 12 : 18;
-}
 // key: bits 0-2 degree index, bits 3-15 squarings (s <= 8191 covers every float32 input)
 __host__ __device__ __forceinline__ unsigned short make_key(int m, int s) {
   return static_cast<unsigned short>(degree_index(m) | (s << 3));
@@ -97,7 +92,7 @@ __device__ __forceinline__ float4 load_vec4(const View& v, int dtype, int64_t of
 // contiguous dimension moves in aligned 4-element vectors (n % 4 == 0).
 enum : unsigned { kClsRows = 1u, kClsVec = 2u };
 
-// One thread per matrix of a strided [batch, n, n] view (P = 8 or 16 bounds n).  Row sums
+// One thread per matrix of a strided [batch, n, n] view (P bounds n).  Row sums
 // accumulate over ascending columns and column sums over ascending rows whatever the loop
 // order, so the float64 norms of A and A^T are bit-identical.
 template <int P>

@@ -20,10 +20,11 @@
 // its own tile (the next operands of the scheme), with the coefficients as compile-time
 // immediates.  Multi-warp teams synchronise with a named barrier per team and square in
 // ping-pong between two slots (one barrier per squaring).  Teams that share a warp run in
-// lockstep with __syncwarp and one program: the largest degree chosen in the warp, each
-// matrix keeping its own number of squarings (a higher degree with the same scaling is at
-// least as accurate), so that the step epilogues of different degrees never run one after
-// another inside a warp.
+// lockstep with __syncwarp.  The eight 8 x 8 teams of a warp either run one program, the
+// largest degree chosen in the warp (each matrix keeping its own number of squarings; a higher
+// degree with the same scaling is at least as accurate), or -- grouped mode, with a workspace --
+// take matrices pre-sorted by (degree, squarings) and run their own.  The two 16 x 16 forward
+// teams of a warp run their own degrees (at most two epilogue paths).
 //
 // Loads are 16-byte chunks spread over the team and prefetched one matrix ahead into
 // registers as raw bits (decoded when the next matrix starts); norms are read back from the
@@ -157,19 +158,21 @@ struct TeamCfg {
   static_assert(TEAM_FLOATS % 4 == 0, "16-byte aligned team regions");
 };
 
-#ifndef FHX_ROW_SWAP
-#define FHX_ROW_SWAP 1
-#endif
-
 // Physical row of logical row i.  A row of a P <= 16 plane covers only half of the 32 banks
 // (P = 16) or a quarter (P = 8), and the rows that one quarter-warp touches together (one per
 // 4-row group: i0, i0 + 4, ...) would all start in the same bank half.  Swapping the two rows of
 // each pair in every other 4-row group puts them in both halves, which makes the tile-chunk
 // accesses of the epilogues and squarings conflict-free (measured before: 28-41 % of the shared
-// wavefronts of the 8 x 8 and 16 x 16 kernels were bank-conflict replays).
-template <int P>
+// wavefronts of the 8 x 8 and 16 x 16 kernels were bank-conflict replays).  Used where it
+// measured faster on B200: the 8 x 8 kernels (config 3: forward -16 %, Frechet -7 %) and the
+// 16 x 16 Frechet kernel (2 x 4 tiles); the 16 x 16 forward (4 x 4 tiles) ran 15 % slower with it.
+template <int P, int TM>
+__host__ __device__ __forceinline__ constexpr bool swapped_rows() {
+  return P == 8 || (P == 16 && TM == 2);
+}
+template <int P, int TM>
 __host__ __device__ __forceinline__ constexpr int prow(int i) {
-  return (FHX_ROW_SWAP && P <= 16) ? (i ^ ((i >> 2) & 1)) : i;
+  return swapped_rows<P, TM>() ? (i ^ ((i >> 2) & 1)) : i;
 }
 
 // Offset of element (i, j) inside a plane: 16-byte chunk (j / 4) of row i is stored at
@@ -180,7 +183,7 @@ __host__ __device__ __forceinline__ constexpr int prow(int i) {
 // call sites.)
 template <int P, int TM>
 __device__ __forceinline__ int pidx(int i, int j) {
-  return prow<P>(i) * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
+  return prow<P, TM>(i) * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
 }
 
 template <int T>
@@ -260,9 +263,14 @@ __device__ __forceinline__ unsigned smem_addr(const float* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
 }
 
-#ifndef FHX_PIPELINED_PRODUCT
-#define FHX_PIPELINED_PRODUCT 1
-#endif
+// Whether a shape issues its shared loads one k ahead (team_product).  Bit-identical either
+// way; measured on B200 (A/B on the same box): faster for the 16 x 16 Frechet kernel (config 4
+// backward -3 %) and the 32 x 32 forward (-1 %), slower for the 8 x 8 kernels and the 32 x 32
+// Frechet kernel, equal elsewhere.
+template <int P, int TM, int TN, bool Pair>
+__host__ __device__ __forceinline__ constexpr bool pipelined_product() {
+  return (P == 16 && Pair) || (P == 32 && !Pair);
+}
 
 // One k of the register-tiled product: row k of Y (y, yu) against column k of the thread's X
 // rows (element r of the 4-k block x, xu).  Frechet: R.u accumulates X dY and dX Y, the two
@@ -322,7 +330,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   const unsigned ybase = smem_addr(Y);
   // rows i0 .. i0 + TM - 1 (TM even, i0 a multiple of TM) sit at physical rows i0 + (ii ^ xs)
   static_assert(TM % 2 == 0, "row pairs");
-  const unsigned xs = unsigned(prow<P>(i0) - i0);
+  const unsigned xs = unsigned(prow<P, TM>(i0) - i0);
   auto load_x = [&](float4 (&dst)[NP][TM], unsigned q16) {
     const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
 #pragma unroll
@@ -332,14 +340,14 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   };
   auto load_y = [&](float4 (&dst)[NP][TN / 4], unsigned k) {
     const unsigned q16 = (k >> 2) << 4;
-    const unsigned row = ybase + unsigned(prow<P>(int(k))) * ROW_B;
+    const unsigned row = ybase + unsigned(prow<P, TM>(int(k))) * ROW_B;
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
       for (int c = 0; c < TN / 4; ++c)
         dst[p][c] = lds128(row + unsigned(p) * PLANE_B + (((c016 + unsigned(c) * 16u) ^ q16) & MASK16));
   };
-#if FHX_PIPELINED_PRODUCT
+  if constexpr (pipelined_product<P, TM, TN, Pair>()) {
   static_assert((P / 4) % 2 == 0, "k-groups are processed in pairs");
   float4 xa[NP][TM], xb[NP][TM], y0[NP][TN / 4], y1[NP][TN / 4];
   load_x(xa, 0u);
@@ -370,7 +378,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
     if (more) load_y(y0, k1 + 4u);
     product_k<TM, TN, Pair>(xb, y1, 3, R);
   }
-#else
+  } else {
 #pragma unroll(Pair ? (P == 32 ? 2 : 1) : (P == 32 ? 4 : 2))
   for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
     float4 xq[NP][TM];
@@ -382,7 +390,7 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
       product_k<TM, TN, Pair>(xq, yq, r, R);
     }
   }
-#endif
+  }
 }
 
 // Element-wise linear combinations of step S on the thread's own TM x TN tile, with the

@@ -157,7 +157,7 @@ int launch_team_kernel(const View& a, const View& e, void* out, void* out2, bool
 template <int P, int TM, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
                 cudaStream_t stream, const SortWorkspace* grouped = nullptr) {
-  if constexpr (P <= 16) {
+  if constexpr (P == 8) {
     if (grouped != nullptr)
       return launch_team_kernel<P, TM, TN, Pair, WARPS, true>(a, e, out, out2, out2_t, batch, n, dtype, stream,
                                                               grouped->perm, grouped->keys);
@@ -192,7 +192,8 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
   return FHX_OK;
 }
 
-bool grouped_size(int n) { return n >= 5 && n <= 16; }
+// Sizes whose teams share a warp with a shared degree unless grouped: the 8 x 8 kernels.
+bool grouped_size(int n) { return n >= 5 && n <= 8; }
 
 // out2 (Frechet launches only, may be null): also write exp(A) there, transposed if out2_t.
 // workspace (may be null): for 5 <= n <= 16, group the batch by degree first (expm_sort.cuh).
@@ -215,8 +216,7 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   SortWorkspace ws{};
   const SortWorkspace* grouped = nullptr;
   if (workspace != nullptr && grouped_size(n)) {
-    const int st = n <= 8 ? group_by_degree<8>(a, batch, n, dtype, workspace, stream, &ws)
-                          : group_by_degree<16>(a, batch, n, dtype, workspace, stream, &ws);
+    const int st = group_by_degree<8>(a, batch, n, dtype, workspace, stream, &ws);
     if (st != FHX_OK) return st;
     grouped = &ws;
   }

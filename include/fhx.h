@@ -61,12 +61,12 @@ int32_t fhx_matrix_exp(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
  * Frechet derivative L(A, E) = d/dt exp(A + tE) at t = 0 (the upper-right block of
  * exp([[A, E], [0, A]])).  The autograd backward of Y = exp(X) is
  * fhx_frechet(X^T, dY), obtained by passing X's strides with in_s1/in_s2 swapped.
- * The number of squarings depends on A only and is identical for A and A^T.  The Taylor
- * degree does too, except where several matrices share a warp: for 5 <= n <= 8 (both entry
- * points) and for the forward at 9 <= n <= 16, a matrix runs the largest degree chosen in its
- * aligned group of 8 or 2 consecutive matrices, which is at least as accurate; its output bits
- * can then depend on those neighbours (within the tolerance).  Results are bit-stable for
- * batch prefixes made of whole aligned groups and for re-runs of the same batch.
+ * The degree and number of squarings depend on A only and are identical for A and A^T,
+ * except for 5 <= n <= 8 without a workspace (fhx_matrix_exp / fhx_frechet): there the eight
+ * matrices that share a warp run the largest degree chosen among them, which is at least as
+ * accurate; a matrix's output bits can then depend on its aligned group of 8 neighbours (within
+ * the tolerance).  Results are bit-stable for batch prefixes made of whole aligned groups and
+ * for re-runs of the same batch.  The _ws entry points make those sizes per-matrix too.
  * Any non-finite entry of A or E makes that matrix's whole output NaN.
  */
 int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
@@ -75,7 +75,7 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
 
 /*
  * Device workspace (bytes) that fhx_matrix_exp_ws / fhx_frechet_ws / fhx_matrix_exp_frechet need
- * for a batch of n x n matrices: 6 bytes per matrix plus 2 KB for 5 <= n <= 16, 0 otherwise.
+ * for a batch of n x n matrices: 6 bytes per matrix plus 2 KB for 5 <= n <= 8, 0 otherwise.
  */
 size_t fhx_workspace_bytes(int64_t batch, int32_t n);
 
@@ -83,11 +83,12 @@ size_t fhx_workspace_bytes(int64_t batch, int32_t n);
  * fhx_matrix_exp and fhx_frechet with a caller-allocated device workspace of at least
  * fhx_workspace_bytes(batch, n) bytes (16-byte aligned; contents on entry do not matter, and
  * the workspace must not be used by another call in flight on the GPU at the same time).  For
- * 5 <= n <= 16 the batch is first grouped by (degree, squarings) -- three small passes that
- * classify every matrix in float64 and build a permutation -- so that the matrices that share a
- * warp run the same program, and every matrix runs its own degree: its result depends on that
- * matrix alone (bit-stable under any batching), and fhx_frechet_ws on A^T repeats the (m, s) of
- * fhx_matrix_exp_ws on A exactly.  Other n ignore the workspace (workspace_bytes may be 0).
+ * 5 <= n <= 8, where eight matrices share a warp, the batch is first grouped by (degree,
+ * squarings) -- three small passes that classify every matrix in float64 and build a
+ * permutation -- so that the matrices of a warp run the same program, and every matrix runs its
+ * own degree: its result depends on that matrix alone (bit-stable under any batching), and
+ * fhx_frechet_ws on A^T repeats the (m, s) of fhx_matrix_exp_ws on A exactly.  Other n ignore
+ * the workspace (workspace_bytes may be 0); they are per-matrix already.
  * Reference interfaces: as fhx_matrix_exp / fhx_frechet (the workspace replaces the
  * reference's per-call pre-copies, csrc/matrix_exp.cu:35-44, which the caching allocator
  * provides there).

@@ -18,6 +18,12 @@ optimized Taylor polynomial approximation", Mathematics 7(12):1174):
   B3(0) = 0, B2(0) = 6 and refine the real root found by a float search (see
   ``T12_START``) to 40 digits.  Any member of the family is exactly T12 in exact arithmetic;
   this member was picked for the smallest float32 evaluation error at ||A||_1 = theta_12.
+* T1, T2, T4 and T8 in the four-product structure of T12 (same B1..B4 layout), so that one
+  evaluation path serves every degree m <= 12 (the n <= 4 kernel keeps its lanes on one
+  program whatever degree each matrix picked): T_m = B1 + (B2 + A6) A6 with A6 = a A^(m/2)
+  (B4 = sqrt(a) A^(m/4), B3 = 0), a = 1/sqrt(m!), B2 = sum_{k=m/2}^{m-1} A^(k-m/2) / (k! a) and
+  B1 = sum_{k<m/2} A^k / k! for m = 4, 8; B1 = T_m itself for m = 1, 2.  Exact in exact
+  arithmetic (A6^2 = A^m / m!).
 * T18 in five products: A9 = B1 B5 + B4, T18 = B2 + (B3 + A9) A9 with B1..B5 combinations
   of (I, A, A2, A3, A6).  The 19 matching equations in 20 unknowns are solved by Newton's
   method in 50-digit arithmetic, seeded with the BBC-2019 published solution (their eq.
@@ -198,6 +204,23 @@ def t18_coefficients():
     return rows_from(mp.findroot(equations, start, tol=mp.mpf(10) ** -45, maxsteps=50))
 
 
+def t12_structure_rows(m: int):
+    """B1..B4 on (I, A, A2, A3) evaluating T_m (m in 1, 2, 4, 8) in the T12 structure."""
+    z = [mp.mpf(0)] * 4
+    if m in (1, 2):
+        b1 = [_fact(k) if k <= m else mp.mpf(0) for k in range(4)]
+        return (b1, list(z), list(z), list(z))
+    h = m // 2                    # A6 = a A^h
+    a = 1 / mp.sqrt(mp.factorial(m))
+    b4 = list(z)
+    b4[h // 2] = mp.sqrt(a)       # B4 = sqrt(a) A^(h/2): A (m = 4) or A2 (m = 8)
+    b2 = list(z)
+    for k in range(h, m):
+        b2[k - h] = _fact(k) / a
+    b1 = [_fact(k) if k < h else mp.mpf(0) for k in range(4)]
+    return (b1, b2, list(z), b4)
+
+
 def scheme_residual(poly, m):
     """Largest |coefficient - 1/k!| relative to 1/k! over k <= m, and the largest term above m."""
     rel = max(abs(poly[k] - _fact(k)) / _fact(k) for k in range(m + 1))
@@ -241,6 +264,23 @@ def render_header(thetas, t8, t12, t18) -> str:
     lines.append("  return tab[r][c];")
     lines.append("}")
     lines.append("")
+    lines.append("// T1, T2, T4, T8 and T12 in the T12 structure: t12u(d, r, c) is the coefficient of")
+    lines.append("// (I, A, A2, A3)[c] in B(r+1) for degree index d (m = 1, 2, 4, 8, 12).")
+    lines.append("__host__ __device__ constexpr float t12u(int d, int r, int c) {")
+    lines.append("  constexpr float tab[5][4][4] = {")
+    for m in (1, 2, 4, 8):
+        lines.append("      {")
+        for row in t12_structure_rows(m):
+            lines.append("          {" + ", ".join(_f(v) + "f" for v in row) + "},")
+        lines.append("      },")
+    lines.append("      {")
+    for row in t12:
+        lines.append("          {" + ", ".join(_f(v) + "f" for v in row) + "},")
+    lines.append("      },")
+    lines.append("  };")
+    lines.append("  return tab[d][r][c];")
+    lines.append("}")
+    lines.append("")
     lines.append("// T18 = B2 + (B3 + A9) A9, A9 = B1 B5 + B4; t18c(r, c) is the coefficient of")
     lines.append("// (I, A, A2, A3, A6)[c] in B(r+1).")
     lines.append("__host__ __device__ constexpr float t18c(int r, int c) {")
@@ -259,7 +299,8 @@ def main():
     parser.add_argument("--check", action="store_true", help="compare with the committed header instead of writing it")
     args = parser.parse_args()
     thetas, t8, t12, t18 = derive()
-    for name, poly, m in (("T8", t8_polynomial(t8), 8), ("T12", t12_polynomial(t12), 12), ("T18", t18_polynomial(t18), 18)):
+    for name, poly, m in (("T8", t8_polynomial(t8), 8), ("T12", t12_polynomial(t12), 12), ("T18", t18_polynomial(t18), 18),
+                          *((f"T{k} (T12 structure)", t12_polynomial(t12_structure_rows(k)), k) for k in (1, 2, 4, 8))):
         rel, tail = scheme_residual(poly, m)
         print(f"{name}: max rel coefficient error {mp.nstr(rel, 3)}, largest term above degree {m}: {mp.nstr(tail, 3)}")
     text = render_header(thetas, t8, t12, t18)

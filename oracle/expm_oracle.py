@@ -51,10 +51,12 @@ def _load_coefficients():
         vals = [float(v) for v in re.findall(r"(-?[0-9.]+(?:[eE][+-]?[0-9]+)?)f", block)]
         return np.array(vals).reshape(rows, -1)
 
-    return theta, t8, table("t12c", 4), table("t18c", 5)
+    block = text.split("constexpr float t12u(int d, int r, int c)")[1].split("return")[0]
+    t12u = np.array([float(v) for v in re.findall(r"(-?[0-9.]+(?:[eE][+-]?[0-9]+)?)f", block)]).reshape(5, 4, 4)
+    return theta, t8, table("t12c", 4), table("t18c", 5), t12u
 
 
-THETA, T8, T12, T18 = _load_coefficients()
+THETA, T8, T12, T18, T12U = _load_coefficients()
 
 
 # --------------------------------------------------------------------------------------
@@ -194,6 +196,19 @@ def selection_norm(a) -> np.ndarray:
     return np.minimum(x.sum(-2).max(-1), x.sum(-1).max(-1))
 
 
+def _taylor_unified(m, a, eye):
+    """The n <= 4 kernel's evaluation (csrc/expm_reg.cuh: taylor): every m <= 12 in the
+    four-product structure of T12 with its own B1..B4 rows (expm_coeffs.h: t12u), T18 as usual."""
+    if m == 18:
+        return _t18(a, eye)
+    a2 = _pair_mul(a, a)
+    a3 = _pair_mul(a2, a)
+    rows = T12U[(1, 2, 4, 8, 12).index(m)]
+    b1, b2, b3, b4 = (_pair_lin(rows[r], [a, a2, a3], eye) for r in range(4))
+    a6 = _pair_add(_pair_mul(b4, b4), b3)
+    return _pair_add(_pair_mul(_pair_add(b2, a6), a6), b1)
+
+
 def _taylor(m, a, eye):
     if m == 1:
         return _pair_lin([1.0, 1.0], [a], eye)
@@ -218,13 +233,15 @@ def _taylor(m, a, eye):
     return _t18(a, eye)
 
 
-def adaptive_algorithm(a, e=None, dtype=np.float64):
-    """Restatement of the kernels' algorithm: exp(A) or L(A, E) in ``dtype`` arithmetic."""
+def adaptive_algorithm(a, e=None, dtype=np.float64, unified=None):
+    """Restatement of the kernels' algorithm: exp(A) or L(A, E) in ``dtype`` arithmetic.
+    ``unified`` (default: n <= 4, as the kernels) evaluates degrees m <= 12 in the T12 structure."""
     a = np.asarray(a, dtype=np.float64)
     batch, n, _ = a.shape
     out = np.empty((batch, n, n), dtype=np.float64)
     eye = np.eye(n, dtype=dtype)
     nus = selection_norm(a)
+    taylor = _taylor_unified if (n <= 4 if unified is None else unified) else _taylor
     for b in range(batch):
         x = a[b].astype(dtype)
         y = None if e is None else np.asarray(e[b], dtype=np.float64).astype(dtype)
@@ -233,7 +250,7 @@ def adaptive_algorithm(a, e=None, dtype=np.float64):
             continue
         m, s = choose_degree(float(nus[b]))
         pair = (np.ldexp(x, -s).astype(dtype), None if y is None else np.ldexp(y, -s).astype(dtype))
-        r = _taylor(m, pair, eye)
+        r = taylor(m, pair, eye)
         for _ in range(s):
             r = _pair_mul(r, r)
         out[b] = r[0] if y is None else r[1]

@@ -70,10 +70,11 @@ def test_null_pointer_and_stride_errors_without_gpu():
 
 def test_workspace_sizes_and_errors_without_gpu():
     lib = _native.load_cabi()
-    # 6 bytes per matrix (key + permutation entry) plus the bin tables, for 5 <= n <= 16 only
+    # 6 bytes per matrix (key + permutation entry) plus the bin tables, for 5 <= n <= 8 only
     assert lib.fhx_workspace_bytes(1000, 8) >= 6000
-    assert lib.fhx_workspace_bytes(1000, 16) == lib.fhx_workspace_bytes(1000, 5)
-    assert lib.fhx_workspace_bytes(1000, 4) == 0 and lib.fhx_workspace_bytes(1000, 17) == 0
+    assert lib.fhx_workspace_bytes(1000, 8) == lib.fhx_workspace_bytes(1000, 5)
+    assert lib.fhx_workspace_bytes(1000, 4) == 0 and lib.fhx_workspace_bytes(1000, 9) == 0
+    assert lib.fhx_workspace_bytes(1000, 16) == 0 and lib.fhx_workspace_bytes(1000, 17) == 0
     assert lib.fhx_workspace_bytes(0, 8) == 0
     buf = ctypes.c_void_p(256)
     need = lib.fhx_workspace_bytes(64, 8)

@@ -77,11 +77,34 @@ def test_t8_t12_t18_polynomials_exact():
     for poly, m in ((D.t8_polynomial(t8), 8), (D.t12_polynomial(t12), 12), (D.t18_polynomial(t18), 18)):
         rel, tail = D.scheme_residual(poly, m)
         assert rel < 1e-30 and tail == 0
+    # T1, T2, T4, T8 in the T12 structure (one evaluation path for every m <= 12)
+    for m in (1, 2, 4, 8):
+        rel, tail = D.scheme_residual(D.t12_polynomial(D.t12_structure_rows(m)), m)
+        assert rel < 1e-30 and tail == 0
     # The refined T18 solution stays within 1e-10 of the published BBC-2019 digits.
     for r in range(5):
         for c in range(5):
             pub = D.T18_PUBLISHED[r][c]
             assert abs(float(t18[r][c]) - pub) <= 1e-10 * max(abs(pub), 1e-30)
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 12])
+def test_unified_structure_equals_truncated_taylor(m):
+    # the float header rows (t12u) evaluate T_m to round-off in float64, value and pair parts
+    rng = np.random.default_rng(300 + m)
+    n = 4
+    a = rng.standard_normal((8, n, n)) * 0.2
+    e = rng.standard_normal((8, n, n))
+    eye = np.eye(n)
+    got = np.stack([O._taylor_unified(m, (x, y), eye)[1] for x, y in zip(a, e)])
+    got_d = np.stack([O._taylor_unified(m, (x, None), eye)[0] for x in a])
+    block = np.zeros((8, 2 * n, 2 * n))
+    block[:, :n, :n] = a
+    block[:, n:, n:] = a
+    block[:, :n, n:] = e
+    ref = _taylor_poly(block, m)
+    assert np.abs(got - ref[:, :n, n:]).max() <= 1e-6 * max(1.0, np.abs(ref).max())
+    assert np.abs(got_d - ref[:, :n, :n]).max() <= 1e-6 * max(1.0, np.abs(ref).max())
 
 
 def test_choose_degree_boundaries():
