@@ -30,7 +30,7 @@ sys.path.insert(0, ROOT)
 
 HEADLINE = 5
 METRIC = "fwd+bwd matrices/s"
-SECONDARY = (2, 4)
+SECONDARY = (2, 3, 4)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "ncu_traffic.json")
 

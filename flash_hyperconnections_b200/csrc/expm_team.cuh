@@ -786,13 +786,15 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
         ncol = maxima[1];
       }
       choose_degree(fmin(nrow, ncol), &m, &s);
-      if constexpr (T < 32) {
-        // Teams that share a warp run one program, of the largest degree chosen in the warp:
+      if constexpr (P == 8) {
+        // The eight teams of a warp run one program, of the largest degree chosen in the warp:
         // the step epilogues of different degrees would otherwise run one after another
         // (measured: 30% of the 8 x 8 Frechet time on mixed-degree batches).  A team keeps its
         // own s, which stays valid for a higher degree (theta_m grows with m), so accuracy never
-        // drops; the degree of a matrix then depends on the aligned group of 32 / T matrices
-        // that shares its warp.
+        // drops; the degree of a matrix then depends on the aligned group of 8 matrices that
+        // shares its warp.  (The grouped mode, with a workspace, avoids both.)  The two teams of
+        // a 16 x 16 forward warp keep their own degrees: at most two epilogue paths, and the
+        // Frechet kernel, whose teams are whole warps, then repeats the forward's (m, s).
         m = int(__reduce_max_sync(0xffffffffu, unsigned(m)));
       }
     }

@@ -32,11 +32,12 @@ def seed():
     torch.manual_seed(9041)
 
 
-def count_fhx_launches(fn) -> int:
-    """Kernels of this package (``fhx::`` device code) that ``fn()`` launches, counted by the
-    CUDA profiler.  Where the profiler records no device activity at all for the launches
-    (CUPTI can drop kernel records after earlier profiling sessions in the same process), the
-    runtime launch calls recorded on the host side are counted instead."""
+def count_fhx_launches(fn, kernels=("fhx::",)) -> int:
+    """Kernels of this package that ``fn()`` launches, counted by the CUDA profiler: device
+    kernels whose name contains one of ``kernels`` (default: every ``fhx::`` kernel).  Where the
+    profiler records no device activity at all (CUPTI can drop kernel records after earlier
+    profiling sessions in the same process), the runtime launch calls recorded on the host side
+    are counted instead, which cannot tell the kernels apart: then every launch counts."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
@@ -45,5 +46,14 @@ def count_fhx_launches(fn) -> int:
     events = prof.key_averages()
     device = [ev for ev in events if str(getattr(ev, "device_type", "")).endswith("CUDA")]
     if device:
-        return sum(int(ev.count) for ev in device if "fhx::" in ev.key)
+        return sum(int(ev.count) for ev in device if any(k in ev.key for k in kernels))
     return sum(int(ev.count) for ev in events if ev.key in ("cudaLaunchKernel", "cudaLaunchKernelExC", "cuLaunchKernel"))
+
+
+# The main kernels (the grouping passes of 5 <= n <= 8 -- classify, scan, scatter -- excluded).
+MAIN_KERNELS = ("expm_team_kernel", "expm_reg_kernel")
+
+
+def grouping_passes(n: int) -> int:
+    """Launches of the degree-grouping passes that precede the main kernel through the operators."""
+    return 3 if 5 <= n <= 8 else 0
