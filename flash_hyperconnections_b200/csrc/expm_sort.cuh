@@ -48,9 +48,9 @@ struct SortWorkspace {
   unsigned* cursor;
 };
 
-__host__ __forceinline__ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+__host__ __device__ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-__host__ __forceinline__ size_t sort_workspace_bytes(int64_t batch) {
+__host__ __device__ constexpr size_t sort_workspace_bytes(int64_t batch) {
   return align256(size_t(batch) * 2) + align256(size_t(batch) * 4) + 2 * align256(kSortBins * 4);
 }
 

@@ -256,6 +256,46 @@ int check_view(const void* p, int64_t s0, int64_t s1, int64_t s2, int64_t batch)
   return FHX_OK;
 }
 
+// ---- scratch of fhx_matrix_exp_noalloc ----
+// Some callers cannot allocate device memory at all (see include/fhx.h); for them the grouping
+// workspace of the 5 <= n <= 8 path lives in this file-scope array, sized for
+// FHX_NOALLOC_MAX_BATCH matrices (about 6 MiB, held by every GPU that loads the library until
+// the process exits).  In host code the name is only a host-side stand-in for the symbol; the
+// device address comes from cudaGetSymbolAddress, once per device, with that device current.
+constexpr size_t kNoAllocScratchBytes = sort_workspace_bytes(FHX_NOALLOC_MAX_BATCH);
+
+struct NoAllocScratch {
+  bool ready[kMaxDevices] = {};
+  void* ptr[kMaxDevices] = {};
+};
+NoAllocScratch g_noalloc;
+
+}  // namespace
+}  // namespace fhx
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[fhx::kNoAllocScratchBytes];
+
+namespace fhx {
+namespace {
+
+// Device address of g_noalloc_scratch on the current device (looked up on the first call there).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int st = cuda_status(cudaGetDevice(&dev));
+  if (st != FHX_OK) return st;
+  if (dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_noalloc.ready[dev]) {
+    void* p = nullptr;
+    st = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (st != FHX_OK) return st;
+    g_noalloc.ptr[dev] = p;
+    g_noalloc.ready[dev] = true;
+  }
+  *out = g_noalloc.ptr[dev];
+  return FHX_OK;
+}
+
 }  // namespace
 }  // namespace fhx
 
@@ -353,6 +393,26 @@ int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, 
                         exp_transposed != 0, fhx_workspace_bytes(batch, n) ? workspace : nullptr);
 }
 
+int32_t fhx_matrix_exp_noalloc(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                               void* output, int64_t batch, int32_t n, int32_t dtype, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  if (batch > FHX_NOALLOC_MAX_BATCH) return FHX_ERR_NOALLOC_LIMIT;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View none{nullptr, 0, 0, 0, 1.f};
+  void* scratch = nullptr;
+  if (grouped_size(n)) {
+    st = noalloc_scratch(&scratch);
+    if (st != FHX_OK) return st;
+  }
+  return dispatch<false>(a, none, output, batch, n, dtype, static_cast<cudaStream_t>(stream), nullptr, false,
+                         scratch);
+}
+
 const char* fhx_status_string(int32_t status) {
   switch (status) {
     case FHX_OK: return "ok";
@@ -362,6 +422,7 @@ const char* fhx_status_string(int32_t status) {
     case FHX_ERR_STRIDE: return "negative stride";
     case FHX_ERR_CUDA: return "a CUDA runtime call or kernel launch failed (see fhx_last_cuda_error)";
     case FHX_ERR_WORKSPACE: return "workspace smaller than fhx_workspace_bytes(batch, n)";
+    case FHX_ERR_NOALLOC_LIMIT: return "batch larger than FHX_NOALLOC_MAX_BATCH, the limit of fhx_matrix_exp_noalloc";
     default: return "unknown status";
   }
 }

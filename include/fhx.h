@@ -42,8 +42,10 @@ extern "C" {
 #define FHX_ERR_CUDA 5       /* a CUDA runtime call or the kernel launch failed; the
                                 cudaError_t is kept for fhx_last_cuda_error()            */
 #define FHX_ERR_WORKSPACE 6  /* workspace smaller than fhx_workspace_bytes(batch, n)   */
+#define FHX_ERR_NOALLOC_LIMIT 7 /* batch > FHX_NOALLOC_MAX_BATCH in fhx_matrix_exp_noalloc */
 
 #define FHX_MAX_N 32
+#define FHX_NOALLOC_MAX_BATCH (1 << 20) /* matrices per call of fhx_matrix_exp_noalloc      */
 #define FHX_MIX_MAX_N 4      /* streams per token of the fused stream mixing            */
 
 /*
@@ -100,6 +102,27 @@ int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
                        const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2, int32_t dir_negate,
                        void* output, int64_t batch, int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/*
+ * fhx_matrix_exp_ws for callers that cannot allocate device memory.  No counterpart in the
+ * reference (whose operator allocates through PyTorch's caching allocator).  Some callers have
+ * no allocator to call: a plugin inside a host engine that owns all device memory and hands the
+ * plugin only its input and output buffers, or a latency-critical path that must never enter
+ * cudaMalloc (which can synchronize the device and take unbounded time).  This entry point
+ * takes inputs and outputs like fhx_matrix_exp and allocates nothing: for 5 <= n <= 8 its
+ * grouping workspace is a static device array of the library, sized for at most
+ * FHX_NOALLOC_MAX_BATCH matrices (about 6 MiB, held by every GPU that loads the library until
+ * the process exits); other n need no workspace.  Results equal fhx_matrix_exp_ws's.
+ *   - A batch larger than FHX_NOALLOC_MAX_BATCH returns FHX_ERR_NOALLOC_LIMIT (nothing runs).
+ *   - The first call on a device looks up the array's device address there
+ *     (cudaGetSymbolAddress, with that device current); make that first call before any
+ *     stream capture.
+ *   - Every call shares the one array and each call fully rewrites what it reads from it.
+ *     Calls that overlap on the GPU -- on different streams, or from different host threads --
+ *     race on it: issue them in one stream order.
+ */
+int32_t fhx_matrix_exp_noalloc(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                               void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
 
 /*
  * exp(A) and L(A, E) from ONE launch: the Frechet kernel carries the pair (exp, derivative)
