@@ -263,133 +263,81 @@ __device__ __forceinline__ unsigned smem_addr(const float* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
 }
 
-// Whether a shape issues its shared loads one k ahead (team_product).  Bit-identical either
-// way; measured on B200 (A/B on the same box): faster for the 16 x 16 Frechet kernel (config 4
-// backward -3 %) and the 32 x 32 forward (-1 %), slower for the 8 x 8 kernels and the 32 x 32
-// Frechet kernel, equal elsewhere.
-template <int P, int TM, int TN, bool Pair>
-__host__ __device__ __forceinline__ constexpr bool pipelined_product() {
-  return (P == 16 && Pair) || (P == 32 && !Pair);
-}
-
-// One k of the register-tiled product: row k of Y (y, yu) against column k of the thread's X
-// rows (element r of the 4-k block x, xu).  Frechet: R.u accumulates X dY and dX Y, the two
-// updates of an element a whole pass apart.
-template <int TM, int TN, bool Pair>
-__device__ __forceinline__ void product_k(const float4 (&x)[Pair ? 2 : 1][TM], const float4 (&y)[Pair ? 2 : 1][TN / 4],
-                                          int r, Acc<TM, TN, Pair>& R) {
-  float2 yd[TN / 2], yu[TN / 2];
-#pragma unroll
-  for (int c = 0; c < TN / 4; ++c) {
-    yd[2 * c] = make_float2(y[0][c].x, y[0][c].y);
-    yd[2 * c + 1] = make_float2(y[0][c].z, y[0][c].w);
-    if constexpr (Pair) {
-      yu[2 * c] = make_float2(y[1][c].x, y[1][c].y);
-      yu[2 * c + 1] = make_float2(y[1][c].z, y[1][c].w);
-    }
-  }
-#pragma unroll
-  for (int ii = 0; ii < TM; ++ii) {
-    const float xv = f4get(x[0][ii], r);
-    const float2 x2 = make_float2(xv, xv);
-#pragma unroll
-    for (int jj = 0; jj < TN / 2; ++jj) {
-      R.d[ii][jj] = __ffma2_rn(x2, yd[jj], R.d[ii][jj]);
-      if constexpr (Pair) R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
-    }
-  }
-  if constexpr (Pair) {
-#pragma unroll
-    for (int ii = 0; ii < TM; ++ii) {
-      const float xu = f4get(x[1][ii], r);
-      const float2 xu2 = make_float2(xu, xu);
-#pragma unroll
-      for (int jj = 0; jj < TN / 2; ++jj) R.u[ii][jj] = __ffma2_rn(xu2, yd[jj], R.u[ii][jj]);
-    }
-  }
-}
-
 // R += X Y.  X, Y: first (value) plane of a slot; the derivative plane follows at +PLANE.
 // Per group of four k: the TM x 4 block of X (TM 128-bit loads) and, for each of the
-// thread's TN/4 column chunks, rows 4q..4q+3 of Y at one rotated chunk position.
-//
-// Software-pipelined: the shared loads for k + 1 (Y rows) and for the next k-group (X block)
-// are issued before the FMAs of k, into a second register buffer, so that their latency runs
-// under the FMAs instead of stalling them.  Every element accumulates the same FMAs in the same
-// order as an unpipelined loop (bit-identical results).
+// thread's TN/4 column chunks, rows 4q..4q+3 of Y at one rotated chunk position.  The Y
+// addresses of a group are one base register per chunk plus immediate row offsets (a
+// per-k address computation measured 8 % slower on the 32 x 32 kernels).  A variant that
+// issued the loads of k + 1 into a second register buffer before the FMAs of k (software
+// pipelining) measured no faster on any shape: the loop is not latency-bound.
 template <int P, int TM, int TN, bool Pair>
 __device__ __forceinline__ void team_product(const float* __restrict__ X, const float* __restrict__ Y, int i0, int j0,
                                              Acc<TM, TN, Pair>& R) {
   constexpr unsigned PLANE_B = P * P * 4;  // bytes
   constexpr unsigned ROW_B = P * 4;
   constexpr unsigned MASK16 = unsigned(P / 4 - 1) << 4;
-  constexpr int NP = Pair ? 2 : 1;
+  constexpr bool swapped = swapped_rows<P, TM>();
   const unsigned rx16 = unsigned(i0 >> 2) << 4;  // rotation of the thread's X rows (bytes)
   const unsigned c016 = unsigned(j0 >> 2) << 4;  // first column chunk of the tile (bytes)
   const unsigned xrow = smem_addr(X) + unsigned(i0) * ROW_B;
-  const unsigned ybase = smem_addr(Y);
-  // rows i0 .. i0 + TM - 1 (TM even, i0 a multiple of TM) sit at physical rows i0 + (ii ^ xs)
-  static_assert(TM % 2 == 0, "row pairs");
-  const unsigned xs = unsigned(prow<P, TM>(i0) - i0);
-  auto load_x = [&](float4 (&dst)[NP][TM], unsigned q16) {
-    const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int ii = 0; ii < TM; ++ii) dst[p][ii] = lds128(xa + unsigned(p) * PLANE_B + (unsigned(ii) ^ xs) * ROW_B);
-  };
-  auto load_y = [&](float4 (&dst)[NP][TN / 4], unsigned k) {
-    const unsigned q16 = (k >> 2) << 4;
-    const unsigned row = ybase + unsigned(prow<P, TM>(int(k))) * ROW_B;
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int c = 0; c < TN / 4; ++c)
-        dst[p][c] = lds128(row + unsigned(p) * PLANE_B + (((c016 + unsigned(c) * 16u) ^ q16) & MASK16));
-  };
-  if constexpr (pipelined_product<P, TM, TN, Pair>()) {
-  static_assert((P / 4) % 2 == 0, "k-groups are processed in pairs");
-  float4 xa[NP][TM], xb[NP][TM], y0[NP][TN / 4], y1[NP][TN / 4];
-  load_x(xa, 0u);
-  load_y(y0, 0u);
-#pragma unroll 1
-  for (unsigned q = 0; q < unsigned(P / 4); q += 2) {
-    // k-group q (X block in xa); the next group's block goes to xb
-    load_x(xb, (q + 1u) << 4);
-    const unsigned k0 = 4u * q;
-    load_y(y1, k0 + 1u);
-    product_k<TM, TN, Pair>(xa, y0, 0, R);
-    load_y(y0, k0 + 2u);
-    product_k<TM, TN, Pair>(xa, y1, 1, R);
-    load_y(y1, k0 + 3u);
-    product_k<TM, TN, Pair>(xa, y0, 2, R);
-    load_y(y0, k0 + 4u);
-    product_k<TM, TN, Pair>(xa, y1, 3, R);
-    // k-group q + 1 (X block in xb); the group after it (if any) goes to xa
-    const bool more = q + 2u < unsigned(P / 4);
-    if (more) load_x(xa, (q + 2u) << 4);
-    const unsigned k1 = k0 + 4u;
-    load_y(y1, k1 + 1u);
-    product_k<TM, TN, Pair>(xb, y0, 0, R);
-    load_y(y0, k1 + 2u);
-    product_k<TM, TN, Pair>(xb, y1, 1, R);
-    load_y(y1, k1 + 3u);
-    product_k<TM, TN, Pair>(xb, y0, 2, R);
-    if (more) load_y(y0, k1 + 4u);
-    product_k<TM, TN, Pair>(xb, y1, 3, R);
-  }
-  } else {
+  // with swapped rows, rows i0 .. i0 + TM - 1 (TM even, i0 a multiple of TM) sit at physical
+  // rows i0 + (ii ^ xs), and rows 4q + r of Y at 4q + (r ^ (q & 1))
+  static_assert(!swapped || TM % 2 == 0, "row pairs");
+  const unsigned xs = swapped ? unsigned(prow<P, TM>(i0) - i0) : 0u;
+  unsigned yrow = smem_addr(Y);
+  // Frechet: R.u accumulates X dY and dX Y, interleaved per k.
 #pragma unroll(Pair ? (P == 32 ? 2 : 1) : (P == 32 ? 4 : 2))
   for (unsigned q16 = 0; q16 < unsigned(P / 4) * 16u; q16 += 16u) {
-    float4 xq[NP][TM];
-    load_x(xq, q16);
+    const unsigned xa = xrow + ((rx16 ^ q16) & MASK16);
+    float4 xb[TM], xub[TM];
+#pragma unroll
+    for (int ii = 0; ii < TM; ++ii) {
+      const unsigned xo = (swapped ? (unsigned(ii) ^ xs) : unsigned(ii)) * ROW_B;
+      xb[ii] = lds128(xa + xo);
+      if constexpr (Pair) xub[ii] = lds128(xa + PLANE_B + xo);
+    }
+    unsigned ya[TN / 4];
+#pragma unroll
+    for (int c = 0; c < TN / 4; ++c) ya[c] = yrow + (((c016 + unsigned(c) * 16u) ^ q16) & MASK16);
+    const unsigned ys = swapped ? (q16 >> 4) & 1u : 0u;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      float4 yq[NP][TN / 4];
-      load_y(yq, (q16 >> 2) + unsigned(r));
-      product_k<TM, TN, Pair>(xq, yq, r, R);
+      const unsigned yo = (swapped ? (unsigned(r) ^ ys) : unsigned(r)) * ROW_B;
+      float2 y[TN / 2], yu[TN / 2];
+#pragma unroll
+      for (int c = 0; c < TN / 4; ++c) {
+        const float4 v = lds128(ya[c] + yo);
+        y[2 * c] = make_float2(v.x, v.y);
+        y[2 * c + 1] = make_float2(v.z, v.w);
+        if constexpr (Pair) {
+          const float4 w = lds128(ya[c] + PLANE_B + yo);
+          yu[2 * c] = make_float2(w.x, w.y);
+          yu[2 * c + 1] = make_float2(w.z, w.w);
+        }
+      }
+#pragma unroll
+      for (int ii = 0; ii < TM; ++ii) {
+        const float x = f4get(xb[ii], r);
+        const float2 x2 = make_float2(x, x);
+#pragma unroll
+        for (int jj = 0; jj < TN / 2; ++jj) {
+          R.d[ii][jj] = __ffma2_rn(x2, y[jj], R.d[ii][jj]);
+          if constexpr (Pair) R.u[ii][jj] = __ffma2_rn(x2, yu[jj], R.u[ii][jj]);
+        }
+      }
+      if constexpr (Pair) {
+        // second derivative term after every other FMA of this k: the two updates of R.u are
+        // a whole pass apart
+#pragma unroll
+        for (int ii = 0; ii < TM; ++ii) {
+          const float xu = f4get(xub[ii], r);
+          const float2 xu2 = make_float2(xu, xu);
+#pragma unroll
+          for (int jj = 0; jj < TN / 2; ++jj) R.u[ii][jj] = __ffma2_rn(xu2, y[jj], R.u[ii][jj]);
+        }
+      }
     }
-  }
+    yrow += 4u * ROW_B;
   }
 }
 

@@ -231,12 +231,16 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   if constexpr (Pair) {
 #if FHX_FRECHET32_TILE == 4
     return launch_team<32, 4, 4, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+#elif FHX_FRECHET32_TILE == 28
+    return launch_team<32, 2, 8, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
 #else
     return launch_team<32, 2, 4, true, 4>(a, e, out, out2, out2_t, batch, n, dtype, stream);
 #endif
   } else {
 #if FHX_FORWARD32_TILE == 48
     return launch_team<32, 4, 8, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+#elif FHX_FORWARD32_TILE == 84
+    return launch_team<32, 8, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
 #else
     return launch_team<32, 4, 4, false, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
 #endif
