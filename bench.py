@@ -279,6 +279,27 @@ def graph_step_ms(fh, a, g, steps: int, warmup: int, flush: torch.Tensor | None)
     return ms, same
 
 
+def fused_step_ms(fh, a, g, steps: int, warmup: int, flush: torch.Tensor | None):
+    """Device time per call of ``fh.matrix_exp_and_grad`` (forward and backward of exp in one
+    Frechet launch, for a known upstream gradient), and whether its gradient equals the
+    autograd step's bit for bit."""
+    for _ in range(warmup):
+        fh.matrix_exp_and_grad(a, g)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        if flush is not None:
+            flush.add_(1.0)
+        e0.record()
+        fh.matrix_exp_and_grad(a, g)
+        e1.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    _, grad = fh.matrix_exp_and_grad(a, g)
+    _, grad_ref = fwd_bwd(fh, a, g)
+    return ms, bool(torch.equal(grad, grad_ref))
+
+
 # End-to-end pipeline shape (matrices per chunk, streams), measured on B200 over PCIe with
 # config 5: 8192 x 4 gave 5.25 M matrices/s, 32768 x 2 gave 4.45 M, 4096 x 8 gave 5.03 M.
 E2E_CHUNK = 8192
@@ -438,6 +459,7 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
     total_ms, fwd_ms, bwd_ms = time_steps(fh, a, g, steps, warmup, dist, flush)
     digest = result_digest(fh, a, g)
     graph = graph_step_ms(fh, a, g, steps, warmup, flush) if with_graph else None
+    fused = fused_step_ms(fh, a, g, steps, warmup, flush)
     result = {
         "digest": digest,
         "count": count,
@@ -454,6 +476,7 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
     }
     if graph is not None:
         result["graph_ms"], result["graph_matches_eager"] = graph
+    result["fused_ms"], result["fused_grad_matches"] = fused
     if with_e2e:
         e2e_count = min(count, 131072)
         a_host = (a[:e2e_count].mT.contiguous() if cfg.transposed else a[:e2e_count]).cpu().pin_memory()
@@ -622,6 +645,8 @@ def main():
     fwd_ms = dist.max(main_res["fwd_ms"])
     bwd_ms = dist.max(main_res["bwd_ms"])
     # algorithmic work of the whole job (every rank's shard), for the per-GPU roofline
+    fused_ms = dist.max(main_res["fused_ms"])
+    fused_ok = dist.sum(0.0 if main_res["fused_grad_matches"] else 1.0) == 0.0
     fwd_flops = dist.sum(main_res["fwd_flops"])
     bwd_flops = dist.sum(main_res["bwd_flops"])
     sum_steps = dist.sum(main_res["mean_steps"] * main_res["count"])
@@ -665,6 +690,8 @@ def main():
             sub_fwd_flops = dist.sum(r["fwd_flops"]) / dist.world
             sub_bwd_flops = dist.sum(r["bwd_flops"]) / dist.world
             sub_steps = dist.sum(r["mean_steps"] * r["count"])
+            sub_fused = dist.max(r["fused_ms"])
+            sub_fused_ok = dist.sum(0.0 if r["fused_grad_matches"] else 1.0) == 0.0
             ms = sub_total / steps
             extras[sub.name] = {
                 "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms, "n_gpus": dist.world,
@@ -674,6 +701,9 @@ def main():
                 "bwd_tflops_per_gpu": sub_bwd_flops / (sub_bwd * 1e9),
                 "hbm_gbs_per_gpu": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": sub_steps / sub.batch,
                 "l2": r["l2"],
+                "fused_fwd_bwd": {"ms_per_step": sub_fused, "value": sub.batch / (sub_fused / 1e3),
+                                  "grad_matches_autograd": sub_fused_ok,
+                                  "path": "fh.matrix_exp_and_grad: forward and backward in one Frechet launch"},
             }
             if "graph_ms" in r:
                 extras[sub.name]["cuda_graph"] = {
@@ -741,6 +771,10 @@ def main():
                        "mean_products_per_matrix": sum_steps / global_batch},
             "gpu_launches": main_res["launches_per_step"] * args.steps,
             "kernel_ms": {"fwd": fwd_ms / 1.0, "bwd": bwd_ms / 1.0},
+            "fused_fwd_bwd": {"ms_per_step": fused_ms, "value": global_batch / (fused_ms / 1e3),
+                              "grad_matches_autograd": fused_ok,
+                              "path": "fh.matrix_exp_and_grad(x, g): forward and backward of exp in one Frechet launch "
+                                      "(for callers that hold the upstream gradient); not the headline step"},
             "roofline": roofline,
             "clocks": clocks,
         }
