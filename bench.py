@@ -46,6 +46,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the CPU baseline sample")
     p.add_argument("--batch", type=int, default=None,
                    help="use only the first BATCH matrices of the config (small cases for profiling)")
+    p.add_argument("--stream-mix-only", action="store_true",
+                   help="run only the fused stream-mixing leg (with --batch: that many tokens per rank)")
     return p.parse_args()
 
 
@@ -497,13 +499,13 @@ MIX_STREAMS = 4
 MIX_WIDTH = 4096     # residual stream width D (model dimension)
 
 
-def measure_stream_mix(fh, dist, steps, warmup, device):
+def measure_stream_mix(fh, dist, steps, warmup, device, tokens=None):
     """fwd+bwd of Y = exp(H) X per token: the fused kernels (fh.mix_streams) against the unfused
     composition (fh.matrix_exp, then a batched matmul, with autograd through both), bf16, on
     this rank's shard of the tokens.  Inputs are larger than L2."""
     W = workloads_module()
     cfg = W.CONFIGS[2]
-    tokens = MIX_TOKENS // dist.world
+    tokens = min(tokens or MIX_TOKENS, MIX_TOKENS) // dist.world
     start = dist.rank * tokens
     h, _ = W.generate(cfg, start, tokens, device=device)
     gen = torch.Generator(device="cpu")
@@ -542,9 +544,9 @@ def measure_stream_mix(fh, dist, steps, warmup, device):
     del h, x, dy
     torch.cuda.empty_cache()
     return {
-        "workload": f"bf16 H [{MIX_TOKENS}, {MIX_STREAMS}, {MIX_STREAMS}] (config 2 generators) applied to streams "
-                    f"[{MIX_TOKENS}, {MIX_STREAMS}, {MIX_WIDTH}]; fwd + bwd (d streams, d H)",
-        "value": MIX_TOKENS / (out["fused"] / 1e3), "unit": "tokens/s", "ms_per_step": out["fused"],
+        "workload": f"bf16 H [{tokens * dist.world}, {MIX_STREAMS}, {MIX_STREAMS}] (config 2 generators) applied to "
+                    f"streams [{tokens * dist.world}, {MIX_STREAMS}, {MIX_WIDTH}]; fwd + bwd (d streams, d H)",
+        "value": tokens * dist.world / (out["fused"] / 1e3), "unit": "tokens/s", "ms_per_step": out["fused"],
         "unfused_ms_per_step": out["unfused"], "speedup_vs_unfused": out["unfused"] / out["fused"],
         "hbm": {"algorithmic_bytes_per_token": per_token, "achieved_gbs_per_gpu": hbm},
         "unfused": "fh.matrix_exp(H) @ X with autograd (exp launch, batched matmul, Frechet launch, matmul backward)",
@@ -632,6 +634,12 @@ def main():
     torch.cuda.set_device(device)
     dist.init("nccl")
     cfg = W.CONFIGS[args.config]
+    if args.stream_mix_only:
+        res = measure_stream_mix(fh, dist, max(5, args.steps), args.warmup, device, tokens=args.batch)
+        if dist.rank == 0:
+            print(json.dumps({"stream_mix": res}), flush=True)
+        dist.close()
+        return
     sampler = ClockSampler(dist.local_rank) if dist.rank == 0 else None
 
     if sampler:

@@ -52,7 +52,9 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_stream_mix.argtypes = [vp, i64, i64, i64, i32, i32, vp, i64, i64, i32, vp, i64, i32, i64, vp]
     lib.fhx_stream_mix.restype = i32
     lib.fhx_stream_mix_backward.argtypes = [vp, i64, i64, i64, i32, i32, vp, i64, i64, i32, vp, i64, i64, vp, vp,
-                                            i64, i32, i64, vp]
+                                            i64, i32, i64, vp, ctypes.c_size_t, vp]
+    lib.fhx_stream_mix_workspace_bytes.argtypes = [i64, i32]
+    lib.fhx_stream_mix_workspace_bytes.restype = ctypes.c_size_t
     lib.fhx_stream_mix_backward.restype = i32
     lib.fhx_status_string.argtypes = [i32]
     lib.fhx_status_string.restype = ctypes.c_char_p

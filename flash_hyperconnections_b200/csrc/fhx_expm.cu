@@ -435,6 +435,6 @@ int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda
 
 const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
 
-int32_t fhx_abi_version(void) { return 103; }
+int32_t fhx_abi_version(void) { return 104; }
 
 }  // extern "C"

@@ -31,6 +31,11 @@
 namespace fhx {
 
 constexpr int kMixThreads = 256;
+// Forward: three CTAs per SM (at most 85 registers; the exponential's code spills a little)
+// and two 16-byte chunks per lane in flight -- measured 3 % faster than one CTA at 125
+// registers and one chunk (0.748 against 0.772 ms on [65536, 4, 4096] bf16, 0.88 of HBM).
+constexpr int kMixForwardMinBlocks = 3;
+constexpr int kMixUnroll = 2;
 
 // 16-byte chunks of a stream row as floats: V elements per chunk.
 template <typename XT>
@@ -131,7 +136,7 @@ struct Streams {
 // Y[t] = exp(H[t]) X[t]; Y contiguous [tokens, N, D].  vec: every row start is 16-byte
 // aligned and D is a multiple of the chunk width, so rows move in 16-byte chunks.
 template <int N, typename XT>
-__global__ void __launch_bounds__(kMixThreads) stream_mix_kernel(View h, int h_dtype, Streams<XT> x, XT* __restrict__ y,
+__global__ void __launch_bounds__(kMixThreads, kMixForwardMinBlocks) stream_mix_kernel(View h, int h_dtype, Streams<XT> x, XT* __restrict__ y,
                                                                  int64_t tokens, int64_t d, int vec) {
   using C = Chunk<XT>;
   constexpr int V = C::V;
@@ -142,22 +147,35 @@ __global__ void __launch_bounds__(kMixThreads) stream_mix_kernel(View h, int h_d
     const XT* xt = x.data + t * x.s0;
     XT* yt = y + t * N * d;
     if (vec) {
+      // U chunks per lane in flight: all loads of a round issue before its FMAs and stores
+      constexpr int U = kMixUnroll;
 #pragma unroll 1
-      for (int64_t c = int64_t(lane) * V; c < d; c += 32 * V) {
-        float xv[N][V];
+      for (int64_t c0 = int64_t(lane) * V; c0 < d; c0 += 32 * V * U) {
+        float xv[U][N][V];
 #pragma unroll
-        for (int j = 0; j < N; ++j) C::load(xt + j * x.s1 + c, xv[j]);
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + int64_t(u) * 32 * V;
+          if (u == 0 || c < d) {
 #pragma unroll
-        for (int i = 0; i < N; ++i) {
-          float yv[V];
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc = fmaf(e.d[i * N + j], xv[j][v], acc);
-            yv[v] = acc;
+            for (int j = 0; j < N; ++j) C::load(xt + j * x.s1 + c, xv[u][j]);
           }
-          C::store(yt + i * d + c, yv);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + int64_t(u) * 32 * V;
+          if (u > 0 && c >= d) break;
+#pragma unroll
+          for (int i = 0; i < N; ++i) {
+            float yv[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+              float acc = 0.f;
+#pragma unroll
+              for (int j = 0; j < N; ++j) acc = fmaf(e.d[i * N + j], xv[u][j][v], acc);
+              yv[v] = acc;
+            }
+            C::store(yt + i * d + c, yv);
+          }
         }
       }
     } else {
@@ -178,12 +196,15 @@ __global__ void __launch_bounds__(kMixThreads) stream_mix_kernel(View h, int h_d
   }
 }
 
-// dX[t] = exp(H[t])^T dY[t] (contiguous [tokens, N, D]) and dH[t] = L(H[t]^T, dY[t] X[t]^T)
-// (contiguous [tokens, N, N] in H's dtype).  vec: as in the forward, for X, dY and dX.
+// Backward, streaming part: dX[t] = exp(H[t])^T dY[t] (contiguous [tokens, N, D]) and
+// G[t] = dY[t] X[t]^T (float32 [tokens, N, N], the caller's workspace).  vec: as in the forward, for
+// X, dY and dX.  The Frechet derivative dH[t] = L(H[t]^T, G[t]) runs in a second, per-token kernel
+// (stream_mix_dh_kernel): its register footprint in this kernel held the stream to one CTA
+// per SM (measured 1.66 ms, 0.59 of HBM, on [65536, 4, 4096] bf16).
 template <int N, typename XT>
 __global__ void __launch_bounds__(kMixThreads) stream_mix_backward_kernel(View h, int h_dtype, Streams<XT> x,
                                                                           Streams<XT> dy, XT* __restrict__ dx,
-                                                                          void* __restrict__ dh, int64_t tokens,
+                                                                          float* __restrict__ gsum, int64_t tokens,
                                                                           int64_t d, int vec) {
   using C = Chunk<XT>;
   constexpr int V = C::V;
@@ -253,20 +274,35 @@ __global__ void __launch_bounds__(kMixThreads) stream_mix_backward_kernel(View h
     for (int k = 0; k < N * N; ++k)
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) g[k] += __shfl_xor_sync(0xffffffffu, g[k], off);
-    RMat<N, true> p;
+    if (lane < N * N) {
+      float v = g[0];
 #pragma unroll
-    for (int i = 0; i < N; ++i)
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        p.d[i * N + j] = hm.d[j * N + i];
-        p.u[i * N + j] = g[i * N + j];
-      }
-    const RMat<N, true> r = expm_regs<N, true>(p);
-    if (lane == 0) {
-#pragma unroll
-      for (int k = 0; k < N * N; ++k) store_elem(dh, h_dtype, t * (N * N) + k, r.u[k]);
+      for (int k = 1; k < N * N; ++k)
+        if (lane == k) v = g[k];
+      gsum[t * (N * N) + lane] = v;
     }
   }
+}
+
+// dH[t] = L(H[t]^T, G[t]) in H's dtype, one thread per token, with the arithmetic of the n <= 4
+// Frechet kernel (expm_regs).
+template <int N>
+__global__ void __launch_bounds__(kMixThreads) stream_mix_dh_kernel(View h, int h_dtype, const float* __restrict__ gsum,
+                                                                    void* __restrict__ dh, int64_t tokens) {
+  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= tokens) return;
+  const RMat<N, false> hm = load_mix_matrix<N, false>(h, h_dtype, t);
+  RMat<N, true> p;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      p.d[i * N + j] = hm.d[j * N + i];
+      p.u[i * N + j] = gsum[t * (N * N) + i * N + j];
+    }
+  const RMat<N, true> r = expm_regs<N, true>(p);
+#pragma unroll
+  for (int k = 0; k < N * N; ++k) store_elem(dh, h_dtype, t * (N * N) + k, r.u[k]);
 }
 
 }  // namespace fhx

@@ -327,10 +327,13 @@ std::tuple<at::Tensor, at::Tensor> mix_streams_backward_cuda(const at::Tensor& h
   at::Tensor dh = at::empty(h.sizes(), h.options().memory_format(at::MemoryFormat::Contiguous));
   if (dh.numel() == 0) return {dx, dh};
   void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
+  const size_t ws_bytes = fhx_stream_mix_workspace_bytes(h.size(0), static_cast<int32_t>(h.size(1)));
+  at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))}, h.options().dtype(at::kFloat));
   const int32_t status = fhx_stream_mix_backward(
       h.const_data_ptr(), h.stride(0), h.stride(1), h.stride(2), h.is_neg() ? 1 : 0, dtype_code(h),
       xs.const_data_ptr(), xs.stride(0), xs.stride(1), dtype_code(xs), gs.const_data_ptr(), gs.stride(0), gs.stride(1),
-      dx.mutable_data_ptr(), dh.mutable_data_ptr(), h.size(0), static_cast<int32_t>(h.size(1)), x.size(2), stream);
+      dx.mutable_data_ptr(), dh.mutable_data_ptr(), h.size(0), static_cast<int32_t>(h.size(1)), x.size(2),
+      ws.mutable_data_ptr(), ws_bytes, stream);
   TORCH_CHECK(status == FHX_OK, "flash_hypercons stream mixing backward: ", fhx_status_string(status),
               status == FHX_ERR_CUDA ? std::string(" (") + fhx_last_cuda_error_string() + ")" : std::string());
   return {dx, dh};

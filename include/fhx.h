@@ -171,18 +171,26 @@ int32_t fhx_stream_mix(const void* h, int64_t h_s0, int64_t h_s1, int64_t h_s2, 
                        int64_t d, void* stream);
 
 /*
+ * Device workspace (bytes) of fhx_stream_mix_backward: tokens * n * n float32 values.
+ */
+size_t fhx_stream_mix_workspace_bytes(int64_t tokens, int32_t n);
+
+/*
  * Backward of fhx_stream_mix for the upstream gradient dY (x_dtype, element (t, i, c) at
  * dy[t*dy_s0 + i*dy_s1 + c]):
  *   dX[t] = exp(H[t])^T dY[t]                 dx: contiguous [tokens, n, d] in x_dtype
  *   dH[t] = L(H[t]^T, dY[t] X[t]^T)           dh: contiguous [tokens, n, n] in h_dtype
- * exp(H[t]) is recomputed in registers, dY[t] X[t]^T is reduced over d in float32 in a fixed
- * order (deterministic), and the Frechet derivative runs in registers with the arithmetic of
- * fhx_frechet's n <= 4 kernel.
+ * Two launches: a warp per token streams X and dY once, writing dX (exp(H[t]) recomputed in
+ * registers) and G[t] = dY[t] X[t]^T, reduced over d in float32 in a fixed order
+ * (deterministic), into the workspace; then one thread per token computes dH[t] from H[t]^T and
+ * G[t] with the arithmetic of fhx_frechet's n <= 4 kernel.
+ *   workspace        at least fhx_stream_mix_workspace_bytes(tokens, n) bytes, 4-byte aligned
+ *                    (contents on entry do not matter; not shared with a call in flight)
  */
 int32_t fhx_stream_mix_backward(const void* h, int64_t h_s0, int64_t h_s1, int64_t h_s2, int32_t h_negate,
                                 int32_t h_dtype, const void* x, int64_t x_s0, int64_t x_s1, int32_t x_dtype,
                                 const void* dy, int64_t dy_s0, int64_t dy_s1, void* dx, void* dh, int64_t tokens,
-                                int32_t n, int64_t d, void* stream);
+                                int32_t n, int64_t d, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Static description of a status code. */
 const char* fhx_status_string(int32_t status);

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_cabi()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.fhx_abi_version() == 103
+    assert lib.fhx_abi_version() == 104
 
 
 def test_status_strings():

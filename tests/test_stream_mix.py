@@ -2,9 +2,9 @@
 
 Checked against a float64 restatement on the CPU (native float64 exp and products, float64
 autograd for the gradients) with the north-star tolerance: relative Frobenius error <= 1e-5 for
-float32 streams and <= 1e-2 for bfloat16 / float16, for Y, dX and dH.  Also: one launch per
-direction, deterministic backward, non-finite tokens isolated, every layout path (16-byte
-chunks, ragged widths, strided rows, non-unit column strides)."""
+float32 streams and <= 1e-2 for bfloat16 / float16, for Y, dX and dH.  Also: one forward launch
+and two backward launches, deterministic backward, non-finite tokens isolated, every layout path
+(16-byte chunks, ragged widths, strided rows, non-unit column strides)."""
 
 import ctypes
 
@@ -52,7 +52,12 @@ def test_stream_mix_rejects_bad_arguments_without_gpu():
     assert lib.fhx_stream_mix(buf, 16, 4, 1, 0, 9, buf, 32, 8, 0, buf, 4, 4, 8, None) == 2
     assert lib.fhx_stream_mix(None, 16, 4, 1, 0, 0, buf, 32, 8, 0, buf, 4, 4, 8, None) == 3
     assert lib.fhx_stream_mix(buf, 16, 4, 1, 0, 0, buf, -32, 8, 0, buf, 4, 4, 8, None) == 4
-    assert lib.fhx_stream_mix_backward(buf, 16, 4, 1, 0, 0, buf, 32, 8, 0, buf, 32, 8, buf, None, 4, 4, 8, None) == 3
+    assert lib.fhx_stream_mix_backward(buf, 16, 4, 1, 0, 0, buf, 32, 8, 0, buf, 32, 8, buf, None, 4, 4, 8, buf, 256,
+                                       None) == 3
+    # the backward's workspace: tokens * n * n float32 values, checked before any CUDA call
+    assert lib.fhx_stream_mix_workspace_bytes(4, 4) == 4 * 16 * 4
+    assert lib.fhx_stream_mix_backward(buf, 16, 4, 1, 0, 0, buf, 32, 8, 0, buf, 32, 8, buf, buf, 4, 4, 8, buf, 255,
+                                       None) == 6
     assert lib.fhx_stream_mix(None, 0, 0, 0, 0, 0, None, 0, 0, 0, None, 0, 4, 8, None) == 0
 
 
@@ -122,7 +127,7 @@ def test_stream_mix_matches_unfused_composition():
 
 
 @pytest.mark.gpu
-def test_stream_mix_one_launch_each_way_and_deterministic():
+def test_stream_mix_launches_and_deterministic():
     h, x, dy = _inputs(300, 4, 2048, torch.bfloat16, torch.bfloat16)
     hh = h.detach().requires_grad_()
     xx = x.detach().requires_grad_()
@@ -132,7 +137,8 @@ def test_stream_mix_one_launch_each_way_and_deterministic():
         out["y"] = fh.mix_streams(hh, xx)
         out["grads"] = torch.autograd.grad(out["y"], (xx, hh), dy)
 
-    assert count_fhx_launches(step) == 2
+    # one forward kernel; the backward streams once and computes dH in a per-token kernel
+    assert count_fhx_launches(step) == 3
     y, grads = out["y"], out["grads"]
     y2 = fh.mix_streams(hh, xx)
     grads2 = torch.autograd.grad(y2, (xx, hh), dy)
