@@ -131,6 +131,42 @@ __host__ __device__ __forceinline__ int program_offset(int m) {
   return m == 2 ? 0 : m == 4 ? 1 : m == 8 ? 3 : m == 12 ? 6 : 10;
 }
 
+// Last step of the program that contains step S.
+__host__ __device__ constexpr int program_last(int S) { return S == 0 ? 0 : S <= 2 ? 2 : S <= 5 ? 5 : S <= 9 ? 9 : 14; }
+
+__host__ __device__ constexpr bool step_reads(const Step& st, int slot, bool epilogue) {
+  if (!epilogue) return st.x == slot || st.y == slot || st.z == slot;
+  for (int t = 0; t < st.nin; ++t)
+    if (st.in[t] == slot) return true;
+  return false;
+}
+__host__ __device__ constexpr bool step_writes_out(const Step& st, int slot) {
+  for (int o = 0; o < st.nout; ++o)
+    if (st.out[o] == slot) return true;
+  return false;
+}
+
+// Whether the product result of step S must go to its slot r: not when S's own epilogue
+// overwrites r (it reads the result from registers), nor when no later step of the program
+// reads r before writing it (the program's result, slot 0 after the last step, is always
+// kept).  E.g. m = 18: A6 (step 12) and B1 * B5 (step 13) live only in their epilogues.
+__host__ __device__ constexpr bool product_store_needed(int S) {
+  const Step st = step_def(S);
+  if (step_writes_out(st, st.r)) return false;
+  for (int k = S + 1; k <= program_last(S); ++k) {
+    const Step nx = step_def(k);
+    if (step_reads(nx, st.r, false)) return true;
+    if (nx.r == st.r) return false;
+    if (step_reads(nx, st.r, true)) return true;
+    if (step_writes_out(nx, st.r)) return false;
+  }
+  return st.r == 0;
+}
+static_assert(!product_store_needed(12) && !product_store_needed(13) && product_store_needed(14) &&
+                  product_store_needed(11) && !product_store_needed(7) && product_store_needed(8) &&
+                  !product_store_needed(4) && !product_store_needed(0) && product_store_needed(1),
+              "product-store liveness");
+
 
 template <int P, int TM, int TN, bool Pair>
 struct TeamCfg {
@@ -341,12 +377,58 @@ __device__ __forceinline__ void team_product(const float* __restrict__ X, const 
   }
 }
 
+// Whether a kernel shape takes each step's product into its epilogue from registers (and skips
+// the stores product_store_needed rules out).  Measured on B200 against storing every product:
+// 8 x 8 forward and Frechet 2 % faster, 16 x 16 Frechet 0.5 % faster; the 32 x 32 Frechet 1.2 %
+// slower (same registers, other scheduling), and the 16 x 16 forward, held to 96 registers for
+// 20 CTAs per SM, spills with the accumulator live through the epilogue.
+template <int P, int TM, int TN, bool Pair>
+__host__ __device__ constexpr bool feed_product() {
+  return P == 8 || (P == 16 && Pair);
+}
+
+// Whether the element-wise phases (step epilogues, the 2^-s scaling) walk the plane in
+// row-major chunks t, t + T, ... instead of the thread's own tile.  For the 16 x 16 forward (4 x 4
+// tiles, no row swap) the own-tile chunks of a quarter-warp fall on the same banks in pairs
+// (rows 4rb + ii of one ii start in the same bank half), while two consecutive rows of a
+// 16-float plane cover all 32 banks; the team (half a warp) then needs a __syncwarp between the
+// product store and the epilogue.
+template <int P, int TM, int TN, bool Pair>
+__host__ __device__ constexpr bool rowmap_elementwise() {
+  return P == 16 && !Pair;
+}
+static_assert(!(rowmap_elementwise<16, 4, 4, false>() && feed_product<16, 4, 4, false>()),
+              "the product feed needs own-tile epilogues");
+
+// Chunk c (0 <= c < TM * TN / 4) of the element-wise phases: elements (i, j .. j + 3) at plane
+// offset off = pidx(i, j).
+template <int P, int TM, int TN, bool Pair>
+__device__ __forceinline__ void ew_chunk(int c, int t, int i0, int j0, int& i, int& j, int& off) {
+  if constexpr (rowmap_elementwise<P, TM, TN, Pair>()) {
+    // rows t / (P/4) + (T / (P/4)) c, and in each the chunk whose rotated position is t % (P/4):
+    // off = i * P + 4 (t % (P/4)), one base plus an immediate per c
+    constexpr int CPR = P / 4;  // chunks per row
+    constexpr int RSTEP = TeamCfg<P, TM, TN, Pair>::T / CPR;
+    static_assert(TeamCfg<P, TM, TN, Pair>::T * TM * TN == P * P, "row-major map covers the plane");
+    static_assert(!swapped_rows<P, TM>(), "physical rows are logical rows");
+    i = t / CPR + RSTEP * c;
+    j = 4 * ((t % CPR) ^ ((i >> 2) & (CPR - 1)));
+    off = (t / CPR) * P + 4 * (t % CPR) + RSTEP * P * c;
+  } else {
+    i = i0 + c / (TN / 4);
+    j = j0 + 4 * (c % (TN / 4));
+    off = pidx<P, TM>(i, j);
+  }
+}
+
 // Element-wise linear combinations of step S on the thread's own TM x TN tile, with the
 // coefficients of step_def(S) as compile-time constants: zero terms vanish, and each term is
 // one FMA per element with an immediate coefficient (paired FMAs at P <= 16).  Terms are
-// accumulated in the table's order, identity first.
+// accumulated in the table's order, identity first.  The input that is the step's own product
+// (slot r) is taken from the accumulator R, which holds the same values.
 template <int P, int TM, int TN, bool Pair, int S>
-__device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, int j0) {
+__device__ __forceinline__ void epilogue_step(float* __restrict__ team, int t_in_team, int i0, int j0,
+                                              const Acc<TM, TN, Pair>& R) {
   constexpr Step st = step_def(S);
   constexpr int PLANE = P * P;
   constexpr int SLOT = TeamCfg<P, TM, TN, Pair>::SLOT;
@@ -356,15 +438,31 @@ __device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, 
     float4 in[st.nin > 0 ? st.nin : 1][CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const int off = part * PLANE + pidx<P, TM>(i0 + c / (TN / 4), j0 + 4 * (c % (TN / 4)));
+      int i, j, o;
+      ew_chunk<P, TM, TN, Pair>(c, t_in_team, i0, j0, i, j, o);
+      const int off = part * PLANE + o;
 #pragma unroll
-      for (int t = 0; t < st.nin; ++t) in[t][c] = *reinterpret_cast<const float4*>(team + st.in[t] * SLOT + off);
+      for (int t = 0; t < st.nin; ++t) {
+        if (feed_product<P, TM, TN, Pair>() && st.in[t] == st.r) {
+          const int ii = c / (TN / 4), cc = c % (TN / 4);
+          float2 lo = R.d[ii][2 * cc], hi = R.d[ii][2 * cc + 1];
+          if constexpr (Pair) {
+            if (part == 1) {
+              lo = R.u[ii][2 * cc];
+              hi = R.u[ii][2 * cc + 1];
+            }
+          }
+          in[t][c] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+          in[t][c] = *reinterpret_cast<const float4*>(team + st.in[t] * SLOT + off);
+        }
+      }
     }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const int i = i0 + c / (TN / 4);
-      const int j = j0 + 4 * (c % (TN / 4));
-      const int off = part * PLANE + pidx<P, TM>(i, j);
+      int i, j, o;
+      ew_chunk<P, TM, TN, Pair>(c, t_in_team, i0, j0, i, j, o);
+      const int off = part * PLANE + o;
       const int dj = part == 0 ? i - j : -1;  // identity pattern of this chunk (value plane only)
       const float4 id = make_float4(dj == 0 ? 1.f : 0.f, dj == 1 ? 1.f : 0.f, dj == 2 ? 1.f : 0.f, dj == 3 ? 1.f : 0.f);
 #pragma unroll
@@ -431,14 +529,19 @@ __device__ __forceinline__ void epilogue_step(float* __restrict__ team, int i0, 
   }
 }
 
-// The steps that have outputs, dispatched on the runtime step index (inlined: measured faster
-// than an out-of-line call, which moves registers across the call boundary).
+// The end of polynomial step S, dispatched on the runtime step index: the product R to slot r
+// where a later step reads it, then the step's epilogue (inlined: measured faster than an
+// out-of-line call, which moves registers across the call boundary).  Shapes without
+// feed_product store R before the call and use only the epilogues.
 template <int P, int TM, int TN, bool Pair>
-__device__ __forceinline__ void team_epilogue(int step_index, float* __restrict__ team, int i0, int j0) {
+__device__ __forceinline__ void team_epilogue(int step_index, float* __restrict__ team, int t_in_team, int i0, int j0,
+                                              const Acc<TM, TN, Pair>& R) {
+  constexpr int SLOT = TeamCfg<P, TM, TN, Pair>::SLOT;
   switch (step_index) {
-#define FHX_EPI(S)                                                                           \
-  case S:                                                                                    \
-    if constexpr (step_def(S).nout > 0) epilogue_step<P, TM, TN, Pair, S>(team, i0, j0); \
+#define FHX_EPI(S)                                                                                  \
+  case S:                                                                                           \
+    if constexpr (feed_product<P, TM, TN, Pair>() && product_store_needed(S)) acc_store<P, TM, TN, Pair>(team + step_def(S).r * SLOT, i0, j0, R); \
+    if constexpr (step_def(S).nout > 0) epilogue_step<P, TM, TN, Pair, S>(team, t_in_team, i0, j0, R);      \
     break;
     FHX_EPI(0) FHX_EPI(1) FHX_EPI(2) FHX_EPI(3) FHX_EPI(4) FHX_EPI(5) FHX_EPI(6) FHX_EPI(7)
     FHX_EPI(8) FHX_EPI(9) FHX_EPI(10) FHX_EPI(11) FHX_EPI(12) FHX_EPI(13) FHX_EPI(14)
@@ -689,26 +792,29 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
       };
       static_assert(T <= 32 || (P == 32 && T >= 2 * P), "team norm split");
       double nrow = 0.0, ncol = 0.0;
+      // row l with 128-bit loads; same partial sums (element k into ps[k % 4], k ascending)
+      auto row_sum = [&](int l) {
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c4 = 0; c4 < P / 4; ++c4) {
+          const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(l, 4 * c4));
+          ps[0] += fabsf(x.x);
+          ps[1] += fabsf(x.y);
+          ps[2] += fabsf(x.z);
+          ps[3] += fabsf(x.w);
+        }
+        const double sum = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
+        return isfinite(sum) ? sum : line_sum(l, false);
+      };
       if constexpr (T > 32) {
         if (t < P) {
-          // row t with 128-bit loads; same partial sums (element k into ps[k % 4], k ascending)
-          float ps[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int c4 = 0; c4 < P / 4; ++c4) {
-            const float4 x = *reinterpret_cast<const float4*>(team + pidx<P, TM>(t, 4 * c4));
-            ps[0] += fabsf(x.x);
-            ps[1] += fabsf(x.y);
-            ps[2] += fabsf(x.z);
-            ps[3] += fabsf(x.w);
-          }
-          nrow = (double(ps[0]) + double(ps[1])) + (double(ps[2]) + double(ps[3]));
-          if (!isfinite(nrow)) nrow = line_sum(t, false);
+          nrow = row_sum(t);
         } else if (t < 2 * P) {
           ncol = line_sum(t - P, true);
         }
       } else {
         for (int l = t; l < P; l += T) {
-          nrow = fmax(nrow, line_sum(l, false));
+          nrow = fmax(nrow, row_sum(l));
           ncol = fmax(ncol, line_sum(l, true));
         }
       }
@@ -756,29 +862,29 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     const int prog = program_offset(m);
     if constexpr (T <= 32) team_sync<T>(tic);  // every column read is done before tiles are rescaled
 
-    // ---- A / 2^s (own tile), identity for the degree-1 polynomial ----
+    // ---- A / 2^s (the element-wise chunks), identity for the degree-1 polynomial ----
     if (s > 0 || m == 1) {
 #pragma unroll 1
       for (int part = 0; part < C::NPART; ++part) {
 #pragma unroll
-        for (int ii = 0; ii < TM; ++ii)
-#pragma unroll
-          for (int c = 0; c < TN / 4; ++c) {
-            float4* p = reinterpret_cast<float4*>(team + part * C::PLANE + pidx<P, TM>(i0 + ii, j0 + 4 * c));
-            float4 v = *p;
-            v.x = scale_pow2(v.x, s);
-            v.y = scale_pow2(v.y, s);
-            v.z = scale_pow2(v.z, s);
-            v.w = scale_pow2(v.w, s);
-            if (m == 1 && part == 0) {
-              const int dj = (i0 + ii) - (j0 + 4 * c);
-              v.x += dj == 0 ? 1.f : 0.f;
-              v.y += dj == 1 ? 1.f : 0.f;
-              v.z += dj == 2 ? 1.f : 0.f;
-              v.w += dj == 3 ? 1.f : 0.f;
-            }
-            *p = v;
+        for (int c = 0; c < TM * TN / 4; ++c) {
+          int i, j, o;
+          ew_chunk<P, TM, TN, Pair>(c, t, i0, j0, i, j, o);
+          float4* p = reinterpret_cast<float4*>(team + part * C::PLANE + o);
+          float4 v = *p;
+          v.x = scale_pow2(v.x, s);
+          v.y = scale_pow2(v.y, s);
+          v.z = scale_pow2(v.z, s);
+          v.w = scale_pow2(v.w, s);
+          if (m == 1 && part == 0) {
+            const int dj = i - j;
+            v.x += dj == 0 ? 1.f : 0.f;
+            v.y += dj == 1 ? 1.f : 0.f;
+            v.z += dj == 2 ? 1.f : 0.f;
+            v.w += dj == 3 ? 1.f : 0.f;
           }
+          *p = v;
+        }
       }
     }
     // Multi-warp teams skip this barrier when nothing was rescaled (team-uniform condition).
@@ -811,8 +917,19 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
       }
       if (!kPingPong || is_poly) team_sync<T>(tic);
       if (active) {
-        acc_store<P, TM, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
-        if (is_poly && step->nout > 0) team_epilogue<P, TM, TN, Pair>(prog + st, team, i0, j0);
+        if constexpr (feed_product<P, TM, TN, Pair>()) {
+          if (is_poly) {
+            team_epilogue<P, TM, TN, Pair>(prog + st, team, t, i0, j0, R);
+          } else {
+            acc_store<P, TM, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
+          }
+        } else {
+          acc_store<P, TM, TN, Pair>(team + rs * C::SLOT, i0, j0, R);
+          if (is_poly && step->nout > 0) {
+            if constexpr (rowmap_elementwise<P, TM, TN, Pair>()) team_sync<T>(tic);  // other threads' tiles
+            team_epilogue<P, TM, TN, Pair>(prog + st, team, t, i0, j0, R);
+          }
+        }
       }
       team_sync<T>(tic);
       if (!is_poly) cur = rs;
