@@ -114,7 +114,27 @@ __global__ void __launch_bounds__(kSortThreads) classify_kernel(View a, int64_t 
       row[i] += av;
       col[j] += av;
     };
-    if (flags & kClsVec) {
+    if ((flags & kClsVec) && n == P) {
+      // whole matrix: every vector load issued before the first sum (same order of sums below)
+      float4 x[P][P / 4];
+#pragma unroll
+      for (int o = 0; o < P; ++o)
+#pragma unroll
+        for (int q = 0; q < P; q += 4)
+          x[o][q / 4] = load_vec4(a, dtype, rows ? base + o * a.s1 + q * a.s2 : base + q * a.s1 + o * a.s2);
+#pragma unroll
+      for (int o = 0; o < P; ++o) {
+#pragma unroll
+        for (int q = 0; q < P; q += 4) {
+          const float xs[4] = {x[o][q / 4].x, x[o][q / 4].y, x[o][q / 4].z, x[o][q / 4].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (rows) add(o, q + u, xs[u]);
+            else add(q + u, o, xs[u]);
+          }
+        }
+      }
+    } else if (flags & kClsVec) {
       // along the contiguous dimension in 4-element vectors (n % 4 == 0)
 #pragma unroll
       for (int o = 0; o < P; ++o) {

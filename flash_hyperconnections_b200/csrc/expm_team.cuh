@@ -1,10 +1,12 @@
 // Team kernel: padded sizes P = 8, 16, 32 (n = 5..32).
 //
 // A "team" of T = (P/TM) * (P/TN) threads owns one matrix; thread (rb, cb) of the team owns
-// the TM x TN register tile at rows TM*rb.., columns TN*cb...  Teams of 4 threads (P = 8) or
-// 16 threads (P = 16 forward) share a warp; the P = 16 Frechet team is one warp (2 x 4 tiles);
-// at P = 32 a team is two warps (forward, 4 x 4 tiles) or four warps (Frechet, 2 x 4 tiles).  The matrix state lives in five shared-memory plane slots per team;
-// registers hold only the accumulator tile of the product in flight.
+// the TM x TN register tile at rows TM*rb.., columns TN*cb...  Teams of 4 threads (P = 8, 4 x 4
+// tiles), 8 threads (P = 8 grouped Frechet, 2 x 4 tiles) or 16 threads (P = 16 forward) share a
+// warp; the P = 16 Frechet team is one warp (2 x 4 tiles); at P = 32 a team is two warps
+// (forward, 4 x 4 tiles) or four warps (Frechet, 2 x 4 tiles).  The matrix state lives in five
+// shared-memory plane slots per team; registers hold only the accumulator tile of the product
+// in flight.
 //
 // Every polynomial step and every squaring is one product R = X Y (+ Z) of slots X, Y (Z an
 // optional slot added on the way in), computed as a register-tiled outer product: per four
@@ -43,6 +45,10 @@
 namespace fhx {
 
 constexpr int kSlots = 5;
+
+#ifndef FHX_FRECHET8_MINBLOCKS
+#define FHX_FRECHET8_MINBLOCKS 16
+#endif
 
 // Layout flags of a launch (computed on the host from strides, dtype and alignment).
 // A view is moved in 16-byte chunks: four consecutive elements of a row ("row chunks",
@@ -190,7 +196,9 @@ struct TeamCfg {
   static_assert(T < 8 || (RB % QR == 0 && CB % QC == 0 && QR * QC == 8), "quarter-warp tiling");
   // Row blocks of one quarter-warp are RB / QR apart (e.g. 0, 4, 8, 12 of 16), so that with
   // TM = 2 they still fall in different 4-row rotation groups.
-  static_assert(T < 8 || TM * (RB / QR) >= 4 || QR == 1, "quarter rows must span rotation groups");
+  // (At P = 8 a row spans 8 banks: row blocks 2 rows apart, e.g. 0, 2, 4, 6 with TM = 2, still
+  // start in four different bank groups.)
+  static_assert(T < 8 || TM * (RB / QR) >= 4 || QR == 1 || P == 8, "quarter rows must span rotation groups");
   static_assert(TEAM_FLOATS % 4 == 0, "16-byte aligned team regions");
 };
 
@@ -615,10 +623,12 @@ template <int P, int TM, int TN, bool Pair, int WARPS>
 constexpr int team_min_blocks() {
   constexpr int smem = (WARPS * 32 / TeamCfg<P, TM, TN, Pair>::T) * TeamCfg<P, TM, TN, Pair>::TEAM_FLOATS * 4 + 1024;
   // Frechet teams smaller than a warp keep their registers (measured: the bound costs more in
-  // spills than the extra resident warps return).  The 32 x 32 forward runs 8 CTAs (16 warps)
-  // at 128 registers rather than 10 at 96 (measured 3 % faster on config 5: no spills in the
-  // per-matrix phases); the 16 x 16 forward runs 20 CTAs (measured 4 % faster than the shared-
-  // memory bound of 16).  Every other shape gets the shared-memory bound.
+  // spills than the extra resident warps return), except the 8 x 8 Frechet with 2 x 4 tiles,
+  // which fits 128 registers without spills (16 CTAs of one warp).  The 32 x 32 forward runs 8
+  // CTAs (16 warps) at 128 registers rather than 10 at 96 (measured 3 % faster on config 5: no
+  // spills in the per-matrix phases); the 16 x 16 forward runs 20 CTAs (measured 4 % faster than
+  // the shared-memory bound of 16).  Every other shape gets the shared-memory bound.
+  if constexpr (Pair && P == 8 && TM == 2) return FHX_FRECHET8_MINBLOCKS;
   if constexpr (Pair && TeamCfg<P, TM, TN, Pair>::T < 32) return 1;
   if constexpr (P == 32 && !Pair && TM * TN == 16) return 8;
   if constexpr (P == 16 && !Pair) return 20;

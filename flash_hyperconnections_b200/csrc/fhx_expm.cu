@@ -20,6 +20,9 @@
 #ifndef FHX_FORWARD32_TILE
 #define FHX_FORWARD32_TILE 44
 #endif
+#ifndef FHX_FRECHET8_TILE
+#define FHX_FRECHET8_TILE 24
+#endif
 
 namespace fhx {
 
@@ -210,7 +213,10 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   // more warps per SM beat larger per-thread tiles as long as the shared-memory wavefront
   // budget holds.  32 x 32: forward 4 x 4 tiles in two-warp teams (16 warps per SM at 128
   // registers), Frechet 2 x 4 tiles in four-warp teams (20 warps per SM at 40 KB of shared
-  // state per matrix).  8 x 8: 4 x 4 tiles, eight teams per warp.  16 x 16: forward 4 x 4 tiles,
+  // state per matrix).  8 x 8: 4 x 4 tiles, eight teams per warp; the grouped Frechet (with a
+  // workspace) 2 x 4 tiles, four teams per warp (128 registers and 16 warps per SM, 12 % faster
+  // than 4 x 4 tiles at 228 registers and 8 warps; without a workspace the eight matrices of a
+  // warp share one degree, so that kernel keeps the forward's eight teams).  16 x 16: forward 4 x 4 tiles,
   // two teams per warp; Frechet 2 x 4 tiles, one team per warp (20 % faster than 4 x 4 tiles,
   // whose 254 registers left 8 warps per SM).
   SortWorkspace ws{};
@@ -220,6 +226,12 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
     if (st != FHX_OK) return st;
     grouped = &ws;
   }
+#if FHX_FRECHET8_TILE == 24
+  if constexpr (Pair) {
+    if (n <= 8 && grouped != nullptr)
+      return launch_team<8, 2, 4, true, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
+  }
+#endif
   if (n <= 8) return launch_team<8, 4, 4, Pair, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
   if (n <= 16) {
     if constexpr (Pair) {
