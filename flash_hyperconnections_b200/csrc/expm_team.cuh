@@ -209,7 +209,8 @@ struct TeamCfg {
 // accesses of the epilogues and squarings conflict-free (measured before: 28-41 % of the shared
 // wavefronts of the 8 x 8 and 16 x 16 kernels were bank-conflict replays).  Used where it
 // measured faster on B200: the 8 x 8 kernels (config 3: forward -16 %, Frechet -7 %) and the
-// 16 x 16 Frechet kernel (2 x 4 tiles); the 16 x 16 forward (4 x 4 tiles) ran 15 % slower with it.
+// 16 x 16 Frechet kernel (2 x 4 tiles); the 16 x 16 forward (4 x 4 tiles, 96 registers) spilled
+// and ran slower with it (2.97 against 2.38 ms on 1,048,576 matrices).
 template <int P, int TM>
 __host__ __device__ __forceinline__ constexpr bool swapped_rows() {
   return P == 8 || (P == 16 && TM == 2);
