@@ -194,17 +194,15 @@ def fwd_bwd(fh, a, g):
 
 
 def count_our_launches(fh, a, g) -> int:
-    """Kernels of libfhx launched by one step, counted by the CUDA profiler."""
-    from torch.profiler import ProfilerActivity, profile
+    """Kernels of libfhx launched by one step, from the library's own launch counter."""
+    from flash_hyperconnections_b200 import _native
 
-    try:
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fwd_bwd(fh, a, g)
-            torch.cuda.synchronize()
-        counted = sum(int(ev.count) for ev in prof.key_averages() if "fhx" in ev.key)
-    except Exception:  # the CUDA profiler is unavailable (e.g. under ncu)
-        counted = 0
-    return counted if counted > 0 else 2  # one forward and one Frechet launch per step
+    lib = _native.load_cabi()
+    torch.cuda.synchronize()
+    before = lib.fhx_launch_count()
+    fwd_bwd(fh, a, g)
+    torch.cuda.synchronize()
+    return int(lib.fhx_launch_count() - before)
 
 
 def time_steps(fh, a, g, steps: int, warmup: int, dist: Dist, flush: torch.Tensor | None = None):
@@ -247,6 +245,62 @@ def time_steps(fh, a, g, steps: int, warmup: int, dist: Dist, flush: torch.Tenso
     fwd = [e0.elapsed_time(e1) for e0, e1, _ in ev]
     bwd = [e1.elapsed_time(e2) for _, e1, e2 in ev]
     return total, statistics.mean(fwd), statistics.mean(bwd)
+
+
+# Cycles of the spin kernel that precedes each device-only step (about 0.5 ms at 1.9 GHz).
+HOST_LEAD_CYCLES = 1_000_000
+
+
+def kernel_device_us(fh, a, g, flush: torch.Tensor, reps: int = 5) -> dict | None:
+    """Mean device duration of each libfhx kernel of an eager step (L2 flushed before each step),
+    from the CUDA profiler's kernel records: the kernels alone, without the launch and event
+    overhead that event-timed phases of a few microseconds include."""
+    from torch.profiler import ProfilerActivity, profile
+
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(reps):
+                flush.add_(1.0)
+                fwd_bwd(fh, a, g)
+            torch.cuda.synchronize()
+        out = {}
+        for ev in prof.key_averages():
+            if "fhx::" not in ev.key:
+                continue
+            total = getattr(ev, "device_time_total", None)
+            if total is None:
+                total = getattr(ev, "cuda_time_total", 0.0)
+            name = ev.key.split("(")[0].replace("void ", "").replace("fhx::", "")
+            out[name] = round(float(total) / max(1, int(ev.count)), 2)
+        return out or None
+    except Exception:  # the CUDA profiler is unavailable (e.g. under ncu)
+        return None
+
+
+def device_phase_ms(fh, a, g, steps: int, flush: torch.Tensor):
+    """Device time of the forward and backward kernels of one eager step, without host gaps: for
+    small batches the host (Python, dispatcher, autograd engine) takes longer to issue a step than
+    the GPU takes to run it, so events around the phases of `time_steps` also count the GPU waiting
+    for the next launch.  Here a spin kernel after each L2 flush lets the host run ahead, and the
+    events around each phase see only its kernels (plus the launch and event overhead of a few
+    microseconds that separates them).  Medians over the steps."""
+    fwd, bwd = [], []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1, e2 in ev:
+        flush.add_(1.0)
+        torch.cuda._sleep(HOST_LEAD_CYCLES)
+        e0.record()
+        x = a.detach().requires_grad_()
+        y = fh.matrix_exp(x)
+        e1.record()
+        torch.autograd.grad(y, x, g)
+        e2.record()
+    torch.cuda.synchronize()
+    for e0, e1, e2 in ev:
+        fwd.append(e0.elapsed_time(e1))
+        bwd.append(e1.elapsed_time(e2))
+    return statistics.median(fwd), statistics.median(bwd)
 
 
 def graph_step_ms(fh, a, g, steps: int, warmup: int, flush: torch.Tensor | None):
@@ -459,6 +513,12 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         flush = torch.empty(64 * 2**20, dtype=torch.float32, device=device)
     launches = count_our_launches(fh, a, g)
     total_ms, fwd_ms, bwd_ms = time_steps(fh, a, g, steps, warmup, dist, flush)
+    eager_phase_ms = None
+    if flush is not None:
+        # the per-kernel figures without the host gaps that the eager step contains
+        eager_phase_ms = {"fwd": fwd_ms, "bwd": bwd_ms}
+        fwd_ms, bwd_ms = device_phase_ms(fh, a, g, max(steps, 5), flush)
+    kernel_us = kernel_device_us(fh, a, g, flush) if flush is not None else None
     digest = result_digest(fh, a, g)
     graph = graph_step_ms(fh, a, g, steps, warmup, flush) if with_graph else None
     fused = fused_step_ms(fh, a, g, steps, warmup, flush)
@@ -468,6 +528,8 @@ def measure_config(fh, cfg, rank, world, dist, steps, warmup, device, with_e2e, 
         "total_ms": total_ms,
         "fwd_ms": fwd_ms,
         "bwd_ms": bwd_ms,
+        "eager_phase_ms": eager_phase_ms,
+        "kernel_device_us": kernel_us,
         "fwd_flops": fwd_flops,
         "bwd_flops": bwd_flops,
         "launches_per_step": launches,
@@ -705,6 +767,12 @@ def main():
                 "value": sub.batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms, "n_gpus": dist.world,
                 "result_digest": {"y_bits_sum": sub_digest[0], "grad_bits_sum": sub_digest[1]},
                 "fwd_kernel_ms": sub_fwd, "bwd_kernel_ms": sub_bwd,
+                "kernel_ms_note": ("device time of each phase's kernels, a spin kernel letting the host run "
+                                   "ahead (the eager step's phases, host gaps included: eager_phase_ms)"
+                                   if r["eager_phase_ms"] is not None else "device time of each phase of the step"),
+                "eager_phase_ms": ({k: dist.max(v) for k, v in r["eager_phase_ms"].items()}
+                                   if r["eager_phase_ms"] is not None else None),
+                "kernel_device_us": r["kernel_device_us"],
                 "fwd_tflops_per_gpu": sub_fwd_flops / (sub_fwd * 1e9),
                 "bwd_tflops_per_gpu": sub_bwd_flops / (sub_bwd * 1e9),
                 "hbm_gbs_per_gpu": r["bytes"] / (ms * 1e6), "mean_products_per_matrix": sub_steps / sub.batch,
@@ -779,6 +847,7 @@ def main():
                        "mean_products_per_matrix": sum_steps / global_batch},
             "gpu_launches": main_res["launches_per_step"] * args.steps,
             "kernel_ms": {"fwd": fwd_ms / 1.0, "bwd": bwd_ms / 1.0},
+            "kernel_device_us": main_res.get("kernel_device_us"),
             "fused_fwd_bwd": {"ms_per_step": fused_ms, "value": global_batch / (fused_ms / 1e3),
                               "grad_matches_autograd": fused_ok,
                               "path": "fh.matrix_exp_and_grad(x, g): forward and backward of exp in one Frechet launch "

@@ -44,6 +44,10 @@ def load_cabi() -> ctypes.CDLL:
     lib.fhx_matrix_exp_ws.restype = i32
     lib.fhx_frechet_ws.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i64, i32, i32, vp, sz, vp]
     lib.fhx_frechet_ws.restype = i32
+    lib.fhx_frechet_grouped.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i64, i32, i32, vp, sz, vp]
+    lib.fhx_frechet_grouped.restype = i32
+    lib.fhx_launch_count.argtypes = []
+    lib.fhx_launch_count.restype = ctypes.c_uint64
     lib.fhx_matrix_exp_noalloc.argtypes = [vp, i64, i64, i64, i32, vp, i64, i32, i32, vp]
     lib.fhx_matrix_exp_noalloc.restype = i32
     lib.fhx_matrix_exp_frechet.argtypes = [vp, i64, i64, i64, i32, vp, i64, i64, i64, i32, vp, i32, vp, i64, i32, i32,

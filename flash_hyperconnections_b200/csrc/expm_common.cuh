@@ -17,6 +17,8 @@ enum : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 // status of a CUDA runtime result that remembers a failure there (both in fhx_expm.cu).
 extern thread_local cudaError_t g_last_cuda_error;
 int cuda_status(cudaError_t err);
+// Kernels launched by this library in this process (fhx_launch_count; fhx_expm.cu).
+void note_launches(int count);
 
 // A read-only strided [batch, n, n] view; `sign` is -1 for a lazily negated tensor.
 struct View {

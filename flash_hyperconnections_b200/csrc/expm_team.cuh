@@ -720,13 +720,14 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   constexpr bool grouped = Grouped;
   auto fetch = [&](int64_t next_item) {
     int64_t nb = next_item * TPC + tic;
-    const bool ok = nb < batch;
+    bool ok = nb < batch;
     if constexpr (grouped) {
       if (ok) {
         nb = ld_s32(perm + nb);
-        pf_key = ld_u16(keys + nb);
+        ok = nb >= 0 && nb < batch;  // an entry outside the batch (a foreign workspace) is skipped
+        pf_key = ok ? ld_u16(keys + nb) : 0u;
       }
-      pf_b = nb;
+      pf_b = ok ? nb : -1;
     }
 #pragma unroll
     for (int k = 0; k < PER_THREAD; ++k) {
@@ -745,7 +746,7 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
   };
   fetch(blockIdx.x);
   for (int64_t item = blockIdx.x; item * TPC < batch; item += gridDim.x) {
-    const bool valid = item * TPC + tic < batch;
+    const bool valid = item * TPC + tic < batch && (!grouped || pf_b >= 0);
     const int64_t b = grouped ? pf_b : item * TPC + tic;
     const unsigned key = pf_key;
 

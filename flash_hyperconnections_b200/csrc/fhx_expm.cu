@@ -7,6 +7,7 @@
 // un-pads the output with another copy; here the kernels read any strided view in the I/O
 // dtype directly and write the n x n output once.
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 
 #include "expm_common.cuh"
@@ -27,6 +28,10 @@
 namespace fhx {
 
 thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+std::atomic<unsigned long long> g_launches{0};
+
+void note_launches(int count) { g_launches.fetch_add(static_cast<unsigned long long>(count), std::memory_order_relaxed); }
 
 int cuda_status(cudaError_t err) {
   if (err == cudaSuccess) return FHX_OK;
@@ -100,6 +105,7 @@ int launch_reg(const View& a, const View& e, void* out, void* out2, bool out2_t,
   if (out2_t) flags |= 8u;
   if (N == 4 && out2 != nullptr && aligned(out2, row_bytes)) flags |= 16u;
   expm_reg_kernel<N, Pair><<<unsigned(blocks), threads, 0, stream>>>(a, e, out, out2, batch, dtype, flags);
+  note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
@@ -153,6 +159,7 @@ int launch_team_kernel(const View& a, const View& e, void* out, void* out2, bool
   const int blocks = int(items < resident ? items : resident);
   kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, perm, keys, batch, n, dtype,
                                             layout_flags<P>(a, e, out, out2, out2_t, n, dtype, Pair));
+  note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
@@ -189,6 +196,7 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
   classify_kernel<P><<<unsigned(blocks), kSortThreads, 0, stream>>>(a, batch, n, dtype, flags, w);
   scan_bins_kernel<<<1, kSortThreads, 0, stream>>>(w);
   scatter_kernel<<<unsigned(blocks), kSortThreads, 0, stream>>>(batch, w);
+  note_launches(3);
   st = cuda_status(cudaGetLastError());
   if (st != FHX_OK) return st;
   *out = w;
@@ -199,10 +207,12 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
 bool grouped_size(int n) { return n >= 5 && n <= 8; }
 
 // out2 (Frechet launches only, may be null): also write exp(A) there, transposed if out2_t.
-// workspace (may be null): for 5 <= n <= 16, group the batch by degree first (expm_sort.cuh).
+// workspace (may be null): for 5 <= n <= 8, group the batch by degree first (expm_sort.cuh);
+// with reuse_grouping, the workspace already holds that grouping (from a launch on the same
+// matrices or their transposes) and the grouping passes are skipped.
 template <bool Pair>
 int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int dtype, cudaStream_t stream,
-             void* out2 = nullptr, bool out2_t = false, void* workspace = nullptr) {
+             void* out2 = nullptr, bool out2_t = false, void* workspace = nullptr, bool reuse_grouping = false) {
   switch (n) {
     case 2: return launch_reg<2, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
     case 3: return launch_reg<3, Pair>(a, e, out, out2, out2_t, batch, dtype, stream);
@@ -222,8 +232,12 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   SortWorkspace ws{};
   const SortWorkspace* grouped = nullptr;
   if (workspace != nullptr && grouped_size(n)) {
-    const int st = group_by_degree<8>(a, batch, n, dtype, workspace, stream, &ws);
-    if (st != FHX_OK) return st;
+    if (reuse_grouping) {
+      ws = sort_workspace(workspace, batch);
+    } else {
+      const int st = group_by_degree<8>(a, batch, n, dtype, workspace, stream, &ws);
+      if (st != FHX_OK) return st;
+    }
     grouped = &ws;
   }
 #if FHX_FRECHET8_TILE == 24
@@ -388,6 +402,27 @@ int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
                         fhx_workspace_bytes(batch, n) ? workspace : nullptr);
 }
 
+int32_t fhx_frechet_grouped(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                            const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
+                            int32_t dir_negate, void* output, int64_t batch, int32_t n, int32_t dtype,
+                            const void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace fhx;
+  int st = check_common(batch, n, dtype, output);
+  if (st != FHX_OK) return st;
+  st = check_view(input, in_s0, in_s1, in_s2, batch);
+  if (st != FHX_OK) return st;
+  st = check_view(direction, dir_s0, dir_s1, dir_s2, batch);
+  if (st != FHX_OK) return st;
+  if (batch == 0) return FHX_OK;
+  if (workspace_bytes < fhx_workspace_bytes(batch, n) || (workspace == nullptr && workspace_bytes > 0))
+    return FHX_ERR_WORKSPACE;
+  const View a{input, in_s0, in_s1, in_s2, in_negate ? -1.f : 1.f};
+  const View e{direction, dir_s0, dir_s1, dir_s2, dir_negate ? -1.f : 1.f};
+  // the kernels only read the grouping (keys and permutation) of a reused workspace
+  return dispatch<true>(a, e, output, batch, n, dtype, static_cast<cudaStream_t>(stream), nullptr, false,
+                        fhx_workspace_bytes(batch, n) ? const_cast<void*>(workspace) : nullptr, true);
+}
+
 int32_t fhx_matrix_exp_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
                                const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
                                int32_t dir_negate, void* exp_output, int32_t exp_transposed, void* frechet_output,
@@ -447,6 +482,8 @@ int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda
 
 const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
 
-int32_t fhx_abi_version(void) { return 104; }
+int32_t fhx_abi_version(void) { return 105; }
+
+uint64_t fhx_launch_count(void) { return fhx::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

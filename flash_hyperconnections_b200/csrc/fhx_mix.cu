@@ -39,6 +39,7 @@ int launch_forward(const View& h, int h_dtype, const void* x, int64_t x_s0, int6
     case 3: stream_mix_kernel<3, XT><<<blocks, kMixThreads, 0, stream>>>(h, h_dtype, xs, out, tokens, d, vec); break;
     default: stream_mix_kernel<4, XT><<<blocks, kMixThreads, 0, stream>>>(h, h_dtype, xs, out, tokens, d, vec); break;
   }
+  note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
@@ -70,6 +71,7 @@ int launch_backward(const View& h, int h_dtype, const void* x, int64_t x_s0, int
       stream_mix_dh_kernel<4><<<dh_blocks, kMixThreads, 0, stream>>>(h, h_dtype, gsum, dh, tokens);
       break;
   }
+  note_launches(2);
   return cuda_status(cudaGetLastError());
 }
 

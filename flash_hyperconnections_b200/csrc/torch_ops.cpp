@@ -28,6 +28,7 @@
 #include <ATen/ops/matmul.h>
 #include <ATen/ops/zeros_like.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDACachingAllocator.h>
 #include <torch/csrc/autograd/custom_function.h>
 #include <torch/csrc/autograd/forward_grad.h>
 #include <torch/csrc/autograd/python_variable.h>
@@ -62,6 +63,33 @@ at::Tensor workspace_for(const at::Tensor& a) {
   return at::empty({static_cast<int64_t>(bytes)}, a.options().dtype(at::kByte));
 }
 
+// Grouping handoff from the forward to the backward of MatrixExpFunction (5 <= n <= 8, where
+// the operators group the batch by degree first): the forward's _matrix_exp call leaves its
+// workspace -- keys and permutation of the grouping -- here, the autograd context keeps it, and
+// the backward's _frechet call on input^T takes it back (fhx_frechet_grouped).  The backward then
+// skips the three grouping passes and runs every matrix at the (m, s) of the forward.  The
+// classification of A and A^T is identical, so the results equal a fresh grouping's bit for bit.
+// Thread-local, set and taken inside one MatrixExpFunction::forward / ::backward on the same
+// thread, matched on data pointer, batch and n; plain CUDA tensors only.
+struct GroupingHandoff {
+  bool want = false;           // the next _matrix_exp call leaves its workspace
+  at::Tensor ws;               // the workspace left by that call, or the one to reuse
+  const void* data = nullptr;  // the matrices it groups
+  int64_t batch = 0;
+  int64_t n = 0;
+};
+thread_local GroupingHandoff g_handoff;
+
+struct HandoffReset {
+  ~HandoffReset() { g_handoff = GroupingHandoff(); }
+};
+
+bool plain_cuda(const at::Tensor& t) {
+  return t.defined() && t.is_cuda() && t.layout() == at::kStrided &&
+         !t.key_set().has_any(c10::DispatchKeySet({c10::DispatchKey::Python, c10::DispatchKey::PythonTLSSnapshot})) &&
+         t.has_storage();
+}
+
 at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
   check_input(a);
   if (direction != nullptr) {
@@ -75,13 +103,35 @@ at::Tensor run(const at::Tensor& a, const at::Tensor* direction) {
   void* stream = static_cast<void*>(at::cuda::getCurrentCUDAStream().stream());
   const int64_t batch = a.size(0);
   const int32_t n = static_cast<int32_t>(a.size(-1));
-  const at::Tensor ws = workspace_for(a);
+  const bool reuse = direction != nullptr && g_handoff.ws.defined() && g_handoff.data == a.const_data_ptr() &&
+                     g_handoff.batch == batch && g_handoff.n == n;
+  at::Tensor ws;
+  if (reuse) {
+    ws = std::move(g_handoff.ws);
+    g_handoff = GroupingHandoff();
+    // allocated on the forward's stream: keep it from reuse until this launch is done
+    c10::cuda::CUDACachingAllocator::recordStream(ws.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
+  } else {
+    ws = workspace_for(a);
+  }
   void* ws_ptr = ws.defined() ? ws.mutable_data_ptr() : nullptr;
   const size_t ws_bytes = ws.defined() ? static_cast<size_t>(ws.numel()) : 0;
   int32_t status;
   if (direction == nullptr) {
     status = fhx_matrix_exp_ws(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
                                out.mutable_data_ptr(), batch, n, dtype_code(a), ws_ptr, ws_bytes, stream);
+    if (status == FHX_OK && g_handoff.want && ws.defined()) {
+      g_handoff.want = false;
+      g_handoff.ws = ws;
+      g_handoff.data = a.const_data_ptr();
+      g_handoff.batch = batch;
+      g_handoff.n = n;
+    }
+  } else if (reuse) {
+    const at::Tensor& e = *direction;
+    status = fhx_frechet_grouped(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
+                                 e.const_data_ptr(), e.stride(0), e.stride(1), e.stride(2), e.is_neg() ? 1 : 0,
+                                 out.mutable_data_ptr(), batch, n, dtype_code(a), ws_ptr, ws_bytes, stream);
   } else {
     const at::Tensor& e = *direction;
     status = fhx_frechet_ws(a.const_data_ptr(), a.stride(0), a.stride(1), a.stride(2), a.is_neg() ? 1 : 0,
@@ -253,8 +303,14 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
                                .typed<at::Tensor(const at::Tensor&)>();
     at::Tensor out;
     {
-      at::AutoDispatchBelowADInplaceOrView below;
-      out = op.call(input);
+      const HandoffReset reset;
+      g_handoff = GroupingHandoff();
+      g_handoff.want = plain_cuda(input);
+      {
+        at::AutoDispatchBelowADInplaceOrView below;
+        out = op.call(input);
+      }
+      if (g_handoff.ws.defined() && g_handoff.data == input.const_data_ptr()) ctx->saved_data["grouping"] = g_handoff.ws;
     }
     ctx->save_for_backward({input});
     return out;
@@ -271,7 +327,17 @@ struct MatrixExpFunction : public torch::autograd::Function<MatrixExpFunction> {
       return {frechet_reference_python(input.mT(), grad)};
     if (has_tangent(input) || has_tangent(grad)) return {frechet_reference(input.mT(), grad)};
     // With grad mode on (a graph of this backward is being built) the call goes through the
-    // autograd formula of _frechet above; otherwise straight to the kernel.
+    // autograd formula of _frechet above; otherwise straight to the kernel.  The forward's
+    // grouping (if any) goes with it.
+    const HandoffReset reset;
+    const auto grouping = ctx->saved_data.find("grouping");
+    if (grouping != ctx->saved_data.end() && plain_cuda(input) && plain_cuda(grad)) {
+      g_handoff = GroupingHandoff();
+      g_handoff.ws = grouping->second.toTensor();
+      g_handoff.data = input.const_data_ptr();
+      g_handoff.batch = input.size(0);
+      g_handoff.n = input.size(-1);
+    }
     return {frechet_op().call(input.mT(), grad)};
   }
 };

@@ -104,6 +104,23 @@ int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
                        void* stream);
 
 /*
+ * fhx_frechet_ws that reuses the grouping of an earlier fhx_matrix_exp_ws on the same matrices
+ * (or their transposes: the classification of A and A^T is identical), same batch and n.  An
+ * extension without reference counterpart, for the autograd backward: exp(X) on X, then
+ * L(X^T, dY) on X^T, with the forward's workspace kept until the backward.  For 5 <= n <= 8 the
+ * three grouping passes are skipped and every matrix runs the forward's (m, s) from the stored
+ * keys; the kernels only read the workspace.  Results equal fhx_frechet_ws's bit for bit.  The
+ * caller guarantees that the workspace holds that grouping and that the matrices were not
+ * changed in between: a workspace of other matrices gives wrong results (permutation entries
+ * outside [0, batch) are skipped, so nothing is read or written out of bounds).  Other n ignore
+ * the workspace.
+ */
+int32_t fhx_frechet_grouped(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
+                            const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,
+                            int32_t dir_negate, void* output, int64_t batch, int32_t n, int32_t dtype,
+                            const void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * fhx_matrix_exp_ws for callers that cannot allocate device memory.  No counterpart in the
  * reference (whose operator allocates through PyTorch's caching allocator).  Some callers have
  * no allocator to call: a plugin inside a host engine that owns all device memory and hands the
@@ -207,6 +224,13 @@ const char* fhx_last_cuda_error_string(void);
 
 /* ABI version of this library (major * 100 + minor). */
 int32_t fhx_abi_version(void);
+
+/*
+ * Kernels this library has launched in this process (all devices and threads), counted on the
+ * host at each launch.  No reference counterpart: tests and benchmarks read it around a call to
+ * count its launches without the CUDA profiler.
+ */
+uint64_t fhx_launch_count(void);
 
 #ifdef __cplusplus
 }

@@ -32,12 +32,23 @@ def seed():
     torch.manual_seed(9041)
 
 
-def count_fhx_launches(fn, kernels=("fhx::",)) -> int:
-    """Kernels of this package that ``fn()`` launches, counted by the CUDA profiler: device
-    kernels whose name contains one of ``kernels`` (default: every ``fhx::`` kernel).  Where the
-    profiler records no device activity at all (CUPTI can drop kernel records after earlier
-    profiling sessions in the same process), the runtime launch calls recorded on the host side
-    are counted instead, which cannot tell the kernels apart: then every launch counts."""
+def count_fhx_launches(fn, kernels=None) -> int:
+    """Kernels of this package that ``fn()`` launches.  Without ``kernels``: every kernel, from the
+    library's own launch counter (``fhx_launch_count``).  With ``kernels``: device kernels whose
+    name contains one of them, counted by the CUDA profiler; where the profiler records no device
+    activity at all (CUPTI can drop kernel records after earlier profiling sessions in the same
+    process), the runtime launch calls recorded on the host side are counted instead, which cannot
+    tell the kernels apart: then every launch counts."""
+    if kernels is None:
+        from flash_hyperconnections_b200 import _native
+
+        lib = _native.load_cabi()
+        torch.cuda.synchronize()
+        before = lib.fhx_launch_count()
+        fn()
+        torch.cuda.synchronize()
+        return int(lib.fhx_launch_count() - before)
+
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:

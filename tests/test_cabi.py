@@ -18,7 +18,7 @@ DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 def declared_functions():
     text = HEADER.read_text()
-    return re.findall(r"^\s*(?:int32_t|size_t|const char\*)\s+(fhx_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^\s*(?:int32_t|uint64_t|size_t|const char\*)\s+(fhx_\w+)\s*\(", text, flags=re.M)
 
 
 def test_header_declares_entry_points():
@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_cabi()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.fhx_abi_version() == 104
+    assert lib.fhx_abi_version() == 105
 
 
 def test_status_strings():
@@ -81,6 +81,7 @@ def test_workspace_sizes_and_errors_without_gpu():
     # too small a workspace is rejected before any CUDA call
     assert lib.fhx_matrix_exp_ws(buf, 64, 8, 1, 0, buf, 64, 8, 0, buf, need - 1, None) == 6
     assert lib.fhx_frechet_ws(buf, 64, 8, 1, 0, buf, 64, 8, 1, 0, buf, 64, 8, 0, None, 0, None) == 6
+    assert lib.fhx_frechet_grouped(buf, 64, 8, 1, 0, buf, 64, 8, 1, 0, buf, 64, 8, 0, None, 0, None) == 6
     assert b"workspace" in lib.fhx_status_string(6)
 
 

@@ -102,3 +102,58 @@ def test_grouped_nonfinite_and_degree_one():
     assert y[ok].isfinite().all()
     assert torch.equal(y[10], torch.eye(8, device="cuda"))
     assert O.per_matrix_error(y[ok], O.exp_fp64(a[ok])).max() <= O.tolerance("float32", False)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n", [5, 8, 12])
+@pytest.mark.parametrize("layout", ["contiguous", "transposed"])
+def test_backward_reuses_forward_grouping(n, dtype, layout):
+    """The autograd backward takes the forward's grouping (5 <= n <= 8): no grouping pass runs in
+    the backward, and its gradient equals a _frechet call that groups afresh, bit for bit."""
+    from .conftest import count_fhx_launches
+
+    a = _mixed(2000, n, dtype, 21)
+    if layout == "transposed":
+        a = a.contiguous().mT
+    g = torch.randn(2000, n, n).to(dtype).cuda()
+    x = a.detach().requires_grad_()
+    y = fh.matrix_exp(x)
+    grads = []
+    # every kernel of this package in the backward: the Frechet kernel alone (a fresh grouping
+    # would add classify, scan and scatter)
+    launches = count_fhx_launches(lambda: grads.append(torch.autograd.grad(y, x, g)[0]))
+    assert launches == 1, launches
+    fresh = torch.ops.flash_hypercons._frechet(a.mT, g)
+    assert torch.equal(grads[0], fresh)
+    # a second backward of the same graph (retain_graph) reuses it again
+    y2 = fh.matrix_exp(x)
+    (g1,) = torch.autograd.grad(y2, x, g, retain_graph=True)
+    (g2,) = torch.autograd.grad(y2, x, g)
+    assert torch.equal(g1, fresh) and torch.equal(g2, fresh)
+
+
+@pytest.mark.parametrize("n", [5, 8, 12])
+def test_cabi_frechet_grouped(n):
+    """fhx_frechet_grouped on A^T with the workspace of fhx_matrix_exp_ws on A equals
+    fhx_frechet_ws (which groups afresh) bit for bit."""
+    lib = _native.load_cabi()
+    batch = 1500
+    a = _mixed(batch, n, torch.float32, 5)
+    e = torch.randn(batch, n, n).cuda()
+    at = a.mT
+    stream = torch.cuda.current_stream().cuda_stream
+    nws = lib.fhx_workspace_bytes(batch, n)
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device="cuda")
+    ws2 = torch.empty_like(ws)
+    y = torch.empty_like(a)
+    l_reuse = torch.empty_like(a)
+    l_fresh = torch.empty_like(a)
+    assert lib.fhx_matrix_exp_ws(a.data_ptr(), *a.stride(), 0, y.data_ptr(), batch, n, 0, ws.data_ptr(), nws,
+                                 stream) == 0
+    assert lib.fhx_frechet_grouped(at.data_ptr(), *at.stride(), 0, e.data_ptr(), *e.stride(), 0, l_reuse.data_ptr(),
+                                   batch, n, 0, ws.data_ptr(), nws, stream) == 0
+    assert lib.fhx_frechet_ws(at.data_ptr(), *at.stride(), 0, e.data_ptr(), *e.stride(), 0, l_fresh.data_ptr(), batch,
+                              n, 0, ws2.data_ptr(), nws, stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(l_reuse, l_fresh)
+    assert O.per_matrix_error(l_reuse, O.frechet_fp64(at, e)).max() <= O.tolerance("float32", True)

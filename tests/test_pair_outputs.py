@@ -13,7 +13,7 @@ import flash_hypercons as fh
 from flash_hyperconnections_b200 import _native
 from oracle import expm_oracle as O
 
-from .conftest import MAIN_KERNELS, count_fhx_launches, grouping_passes
+from .conftest import count_fhx_launches, grouping_passes
 from .test_routing import op_names
 
 DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
@@ -105,8 +105,8 @@ def test_forward_ad_runs_one_frechet_launch(dtype, n):
     with torch.autograd.forward_ad.dual_level():
         dual = torch.autograd.forward_ad.make_dual(a, e)
         # one Frechet launch (after the grouping passes for 5 <= n <= 8)
-        launches = count_fhx_launches(lambda: fh.matrix_exp(dual), MAIN_KERNELS)
-        assert launches in (1, 1 + grouping_passes(n)), launches
+        launches = count_fhx_launches(lambda: fh.matrix_exp(dual))
+        assert launches == 1 + grouping_passes(n), launches
 
 
 @pytest.mark.gpu
@@ -138,8 +138,8 @@ def test_matrix_exp_and_grad_matches_autograd(dtype, n):
     assert torch.equal(grad, grad_ref)  # same Frechet kernel on the same view a.mT
     assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance(_kind(dtype), False)
     assert O.per_matrix_error(grad, O.frechet_fp64(a.mT, g)).max() <= O.tolerance(_kind(dtype), True)
-    launches = count_fhx_launches(lambda: fh.matrix_exp_and_grad(a, g), MAIN_KERNELS)
-    assert launches in (1, 1 + grouping_passes(n)), launches
+    launches = count_fhx_launches(lambda: fh.matrix_exp_and_grad(a, g))
+    assert launches == 1 + grouping_passes(n), launches
 
 
 def test_matrix_exp_and_grad_cpu_uses_native():
