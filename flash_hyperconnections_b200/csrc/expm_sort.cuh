@@ -1,16 +1,16 @@
 // Degree classification and grouping for the team kernel whose teams share a warp (5 <= n <= 8:
-// eight 4-thread teams per warp).
+// eight 4-thread or four 8-thread teams per warp).
 //
 // Teams in one warp run in lockstep, so a warp costs as much as its most expensive matrix.  On a
 // batch of mixed norms (config 3: degrees 4/8/12/18 in about equal shares, 0-4 squarings) that
 // is 7.4 product steps per 8 x 8 matrix where the matrices themselves need 4.0.  Before the main
-// kernel, three small passes group the batch by cost:
+// kernel, two small passes group the batch by cost:
 //
 //   classify   one thread per matrix: nu = min(||A||_1, ||A||_inf) in float64 (rows and columns
 //              each summed in ascending order, so A and A^T give the same bits), (m, s) by
 //              choose_degree, a 16-bit key per matrix, and a histogram of key bins;
-//   scan       exclusive prefix sum of the histogram (one CTA);
-//   scatter    every matrix's index into its bin's range of a permutation.
+//   scatter    the bin starts (every CTA scans the histogram itself) and every matrix's index
+//              into its bin's range of a permutation.
 //
 // The main kernel then takes its matrices in permutation order and each team runs its matrix's
 // own (m, s) from the key: a matrix's result depends on that matrix alone (no degree shared with
@@ -19,7 +19,8 @@
 // computes which matrix, never a result.
 //
 // Workspace (caller-allocated, fhx_workspace_bytes): keys (2 B per matrix), permutation (4 B per
-// matrix), histogram and bin cursors (kSortBins words each).
+// matrix), histogram and bin cursors (kSortBins words each, adjacent: zeroed by one memset before
+// the classify pass).
 #pragma once
 
 #include "expm_common.cuh"
@@ -181,34 +182,42 @@ __global__ void __launch_bounds__(kSortThreads) classify_kernel(View a, int64_t 
   add_block_histogram(bin, ws.hist, s_cnt);
 }
 
-// Exclusive prefix sum of the histogram into hist (bin starts); cursors to zero.  One CTA.
-__global__ void __launch_bounds__(kSortThreads) scan_bins_kernel(SortWorkspace ws) {
-  __shared__ unsigned s_v[kSortBins];
-  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) {
-    s_v[i] = ws.hist[i];
-    ws.cursor[i] = 0;
+// Exclusive prefix sum of the kSortBins histogram counts into s_start, by every CTA of the scatter
+// pass for itself (a few hundred words; warp-shuffle scans, then the warp totals).
+__device__ __forceinline__ void bin_starts(const unsigned* __restrict__ hist, unsigned* s_start, unsigned* s_warp) {
+  static_assert(kSortBins <= kSortThreads, "one bin per thread");
+  const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+  const unsigned c = i < kSortBins ? hist[i] : 0u;
+  unsigned v = c;  // inclusive scan within the warp
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += o;
   }
+  if (lane == 31) s_warp[warp] = v;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned run = 0;
-    for (int i = 0; i < kSortBins; ++i) {
-      const unsigned c = s_v[i];
-      s_v[i] = run;
-      run += c;
+  if (warp == 0) {
+    unsigned w = lane < kSortThreads / 32 ? s_warp[lane] : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const unsigned o = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += o;
     }
+    if (lane < kSortThreads / 32) s_warp[lane] = w;  // inclusive totals of warps 0..lane
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) ws.hist[i] = s_v[i];
+  if (i < kSortBins) s_start[i] = v - c + (warp > 0 ? s_warp[warp - 1] : 0u);
 }
 
-// perm[start(bin) + rank] = b: a CTA reserves one range per bin with a global atomic and hands
-// out ranks inside it with shared-memory atomics.
+// perm[start(bin) + rank] = b: a CTA reserves one range per bin with a global atomic on the bin's
+// cursor (zero on entry) and hands out ranks inside it with shared-memory atomics.
 __global__ void __launch_bounds__(kSortThreads) scatter_kernel(int64_t batch, SortWorkspace ws) {
   __shared__ unsigned s_cnt[kSortBins];
   __shared__ unsigned s_base[kSortBins];
+  __shared__ unsigned s_warp[kSortThreads / 32];
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) s_cnt[i] = 0;
-  __syncthreads();
+  bin_starts(ws.hist, s_base, s_warp);  // (its barriers also order the zeroing above)
   int bin = -1;
   unsigned local = 0;
   if (b < batch) {
@@ -217,7 +226,7 @@ __global__ void __launch_bounds__(kSortThreads) scatter_kernel(int64_t batch, So
   }
   __syncthreads();
   for (int i = threadIdx.x; i < kSortBins; i += blockDim.x)
-    if (s_cnt[i]) s_base[i] = ws.hist[i] + atomicAdd(&ws.cursor[i], s_cnt[i]);
+    if (s_cnt[i]) s_base[i] += atomicAdd(&ws.cursor[i], s_cnt[i]);
   __syncthreads();
   if (bin >= 0) ws.perm[s_base[bin] + local] = int(b);
 }

@@ -176,13 +176,14 @@ int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t
                                                            nullptr);
 }
 
-// Grouping passes of expm_sort.cuh on the view `a` (5 <= n <= 16): keys, histogram, bin starts,
-// permutation, in the caller's workspace.
+// Grouping passes of expm_sort.cuh on the view `a` (5 <= n <= 8): keys, histogram and permutation in
+// the caller's workspace.
 template <int P>
 int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* workspace, cudaStream_t stream,
                     SortWorkspace* out) {
   const SortWorkspace w = sort_workspace(workspace, batch);
-  int st = cuda_status(cudaMemsetAsync(w.hist, 0, kSortBins * sizeof(unsigned), stream));
+  // histogram and bin cursors (adjacent) to zero
+  int st = cuda_status(cudaMemsetAsync(w.hist, 0, 2 * align256(kSortBins * sizeof(unsigned)), stream));
   if (st != FHX_OK) return st;
   // the contiguous dimension of the view, and whether it moves in aligned 4-element vectors
   const bool rows = a.s2 == 1 || (a.s1 != 1 && a.s2 <= a.s1);
@@ -194,9 +195,8 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
   const int64_t blocks = (batch + kSortThreads - 1) / kSortThreads;
   if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
   classify_kernel<P><<<unsigned(blocks), kSortThreads, 0, stream>>>(a, batch, n, dtype, flags, w);
-  scan_bins_kernel<<<1, kSortThreads, 0, stream>>>(w);
   scatter_kernel<<<unsigned(blocks), kSortThreads, 0, stream>>>(batch, w);
-  note_launches(3);
+  note_launches(2);
   st = cuda_status(cudaGetLastError());
   if (st != FHX_OK) return st;
   *out = w;

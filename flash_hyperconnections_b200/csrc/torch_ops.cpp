@@ -67,7 +67,7 @@ at::Tensor workspace_for(const at::Tensor& a) {
 // the operators group the batch by degree first): the forward's _matrix_exp call leaves its
 // workspace -- keys and permutation of the grouping -- here, the autograd context keeps it, and
 // the backward's _frechet call on input^T takes it back (fhx_frechet_grouped).  The backward then
-// skips the three grouping passes and runs every matrix at the (m, s) of the forward.  The
+// skips the grouping passes and runs every matrix at the (m, s) of the forward.  The
 // classification of A and A^T is identical, so the results equal a fresh grouping's bit for bit.
 // Thread-local, set and taken inside one MatrixExpFunction::forward / ::backward on the same
 // thread, matched on data pointer, batch and n; plain CUDA tensors only.

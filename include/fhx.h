@@ -86,7 +86,7 @@ size_t fhx_workspace_bytes(int64_t batch, int32_t n);
  * fhx_workspace_bytes(batch, n) bytes (16-byte aligned; contents on entry do not matter, and
  * the workspace must not be used by another call in flight on the GPU at the same time).  For
  * 5 <= n <= 8, where eight matrices share a warp, the batch is first grouped by (degree,
- * squarings) -- three small passes that classify every matrix in float64 and build a
+ * squarings) -- two small passes that classify every matrix in float64 and build a
  * permutation -- so that the matrices of a warp run the same program, and every matrix runs its
  * own degree: its result depends on that matrix alone (bit-stable under any batching), and
  * fhx_frechet_ws on A^T repeats the (m, s) of fhx_matrix_exp_ws on A exactly.  Other n ignore
@@ -108,7 +108,7 @@ int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
  * (or their transposes: the classification of A and A^T is identical), same batch and n.  An
  * extension without reference counterpart, for the autograd backward: exp(X) on X, then
  * L(X^T, dY) on X^T, with the forward's workspace kept until the backward.  For 5 <= n <= 8 the
- * three grouping passes are skipped and every matrix runs the forward's (m, s) from the stored
+ * grouping passes are skipped and every matrix runs the forward's (m, s) from the stored
  * keys; the kernels only read the workspace.  Results equal fhx_frechet_ws's bit for bit.  The
  * caller guarantees that the workspace holds that grouping and that the matrices were not
  * changed in between: a workspace of other matrices gives wrong results (permutation entries

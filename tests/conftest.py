@@ -61,10 +61,10 @@ def count_fhx_launches(fn, kernels=None) -> int:
     return sum(int(ev.count) for ev in events if ev.key in ("cudaLaunchKernel", "cudaLaunchKernelExC", "cuLaunchKernel"))
 
 
-# The main kernels (the grouping passes of 5 <= n <= 8 -- classify, scan, scatter -- excluded).
+# The main kernels (the grouping passes of 5 <= n <= 8 -- classify, scatter -- excluded).
 MAIN_KERNELS = ("expm_team_kernel", "expm_reg_kernel")
 
 
 def grouping_passes(n: int) -> int:
     """Launches of the degree-grouping passes that precede the main kernel through the operators."""
-    return 3 if 5 <= n <= 8 else 0
+    return 2 if 5 <= n <= 8 else 0

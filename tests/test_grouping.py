@@ -120,7 +120,7 @@ def test_backward_reuses_forward_grouping(n, dtype, layout):
     y = fh.matrix_exp(x)
     grads = []
     # every kernel of this package in the backward: the Frechet kernel alone (a fresh grouping
-    # would add classify, scan and scatter)
+    # would add classify and scatter)
     launches = count_fhx_launches(lambda: grads.append(torch.autograd.grad(y, x, g)[0]))
     assert launches == 1, launches
     fresh = torch.ops.flash_hypercons._frechet(a.mT, g)
