@@ -93,6 +93,49 @@ __device__ __forceinline__ float4 load_vec4(const View& v, int dtype, int64_t of
 // contiguous dimension moves in aligned 4-element vectors (n % 4 == 0).
 enum : unsigned { kClsRows = 1u, kClsVec = 2u };
 
+// The key of a matrix from its float64 line sums |a| (rows[i], columns[j]) and whether an entry
+// was non-finite.
+template <int P>
+__device__ __forceinline__ unsigned short key_of_sums(const double (&row)[P], const double (&col)[P], bool bad) {
+  double nrow = 0.0, ncol = 0.0;
+#pragma unroll
+  for (int t = 0; t < P; ++t) {
+    nrow = fmax(nrow, row[t]);
+    ncol = fmax(ncol, col[t]);
+  }
+  if (bad) return kKeyBad;
+  int m, s;
+  choose_degree(fmin(nrow, ncol), &m, &s);
+  return make_key(m, s);
+}
+
+// The key of a full P x P matrix given as its 16-byte chunks along the contiguous dimension:
+// x[o][q / 4] = elements q..q+3 of line o (a row if `rows`, else a column).  Row sums accumulate
+// over ascending columns and column sums over ascending rows.
+template <int P>
+__device__ __forceinline__ unsigned short key_of_matrix(const float4 (&x)[P][P / 4], bool rows) {
+  double row[P], col[P];
+#pragma unroll
+  for (int t = 0; t < P; ++t) row[t] = col[t] = 0.0;
+  bool bad = false;
+#pragma unroll
+  for (int o = 0; o < P; ++o) {
+#pragma unroll
+    for (int q = 0; q < P; q += 4) {
+      const float xs[4] = {x[o][q / 4].x, x[o][q / 4].y, x[o][q / 4].z, x[o][q / 4].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = rows ? o : q + u, j = rows ? q + u : o;
+        bad |= !isfinite(xs[u]);
+        const double av = fabs(double(xs[u]));
+        row[i] += av;
+        col[j] += av;
+      }
+    }
+  }
+  return key_of_sums<P>(row, col, bad);
+}
+
 // One thread per matrix of a strided [batch, n, n] view (P bounds n).  Row sums
 // accumulate over ascending columns and column sums over ascending rows whatever the loop
 // order, so the float64 norms of A and A^T are bit-identical.
@@ -103,79 +146,104 @@ __global__ void __launch_bounds__(kSortThreads) classify_kernel(View a, int64_t 
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   int bin = -1;
   if (b < batch) {
-    double row[P], col[P];
-#pragma unroll
-    for (int t = 0; t < P; ++t) row[t] = col[t] = 0.0;
-    bool bad = false;
     const int64_t base = b * a.s0;
     const bool rows = flags & kClsRows;
-    auto add = [&](int i, int j, float v) {
-      bad |= !isfinite(v);
-      const double av = fabs(double(v));
-      row[i] += av;
-      col[j] += av;
-    };
+    unsigned short key;
     if ((flags & kClsVec) && n == P) {
-      // whole matrix: every vector load issued before the first sum (same order of sums below)
+      // whole matrix: every vector load issued before the first sum
       float4 x[P][P / 4];
 #pragma unroll
       for (int o = 0; o < P; ++o)
 #pragma unroll
         for (int q = 0; q < P; q += 4)
           x[o][q / 4] = load_vec4(a, dtype, rows ? base + o * a.s1 + q * a.s2 : base + q * a.s1 + o * a.s2);
+      key = key_of_matrix<P>(x, rows);
+    } else {
+      double row[P], col[P];
 #pragma unroll
-      for (int o = 0; o < P; ++o) {
+      for (int t = 0; t < P; ++t) row[t] = col[t] = 0.0;
+      bool bad = false;
+      auto add = [&](int i, int j, float v) {
+        bad |= !isfinite(v);
+        const double av = fabs(double(v));
+        row[i] += av;
+        col[j] += av;
+      };
+      if (flags & kClsVec) {
+        // along the contiguous dimension in 4-element vectors (n % 4 == 0)
 #pragma unroll
-        for (int q = 0; q < P; q += 4) {
-          const float xs[4] = {x[o][q / 4].x, x[o][q / 4].y, x[o][q / 4].z, x[o][q / 4].w};
+        for (int o = 0; o < P; ++o) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (rows) add(o, q + u, xs[u]);
-            else add(q + u, o, xs[u]);
-          }
-        }
-      }
-    } else if (flags & kClsVec) {
-      // along the contiguous dimension in 4-element vectors (n % 4 == 0)
+          for (int q = 0; q < P; q += 4) {
+            if (o < n && q < n) {
+              const int64_t off = rows ? base + o * a.s1 + q * a.s2 : base + q * a.s1 + o * a.s2;
+              const float4 x = load_vec4(a, dtype, off);
+              const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-      for (int o = 0; o < P; ++o) {
-#pragma unroll
-        for (int q = 0; q < P; q += 4) {
-          if (o < n && q < n) {
-            const int64_t off = rows ? base + o * a.s1 + q * a.s2 : base + q * a.s1 + o * a.s2;
-            const float4 x = load_vec4(a, dtype, off);
-            const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              if (rows) add(o, q + u, xs[u]);
-              else add(q + u, o, xs[u]);
+              for (int u = 0; u < 4; ++u) {
+                if (rows) add(o, q + u, xs[u]);
+                else add(q + u, o, xs[u]);
+              }
             }
           }
         }
+      } else {
+#pragma unroll
+        for (int o = 0; o < P; ++o)
+#pragma unroll
+          for (int q = 0; q < P; ++q)
+            if (o < n && q < n) {
+              // (the sign of a negated view does not change |a|)
+              if (rows) add(o, q, load_elem(a.data, dtype, base + o * a.s1 + q * a.s2));
+              else add(q, o, load_elem(a.data, dtype, base + q * a.s1 + o * a.s2));
+            }
       }
-    } else {
-#pragma unroll
-      for (int o = 0; o < P; ++o)
-#pragma unroll
-        for (int q = 0; q < P; ++q)
-          if (o < n && q < n) {
-            // (the sign of a negated view does not change |a|)
-            if (rows) add(o, q, load_elem(a.data, dtype, base + o * a.s1 + q * a.s2));
-            else add(q, o, load_elem(a.data, dtype, base + q * a.s1 + o * a.s2));
-          }
+      key = key_of_sums<P>(row, col, bad);
     }
-    double nrow = 0.0, ncol = 0.0;
+    ws.keys[b] = key;
+    bin = key_bin(key);
+  }
+  add_block_histogram(bin, ws.hist, s_cnt);
+}
+
+// classify_kernel<8> for a dense float32 batch: matrix b is the 64 floats at a + 64 b, rows or
+// columns contiguous (flags).  One thread per matrix reading its own 256 bytes makes every warp
+// load touch 32 cache lines, which left the general kernel waiting on L1 (about 2.7 TB/s).  Here
+// each warp first copies its 32 matrices (8 KB) into shared memory with fully coalesced 16-byte
+// loads, each matrix padded by 16 bytes so that the 32 threads then read their own matrices
+// without bank conflicts; the sums and keys are those of classify_kernel's whole-matrix path.
+constexpr int kDenseThreads = 128;
+constexpr int kDenseStride = 68;  // floats per matrix in shared memory (64 + 4 of padding)
+
+__global__ void __launch_bounds__(kDenseThreads) classify_dense8_kernel(const float* __restrict__ a, int64_t batch,
+                                                                        unsigned flags, SortWorkspace ws) {
+  __shared__ __align__(16) float s_m[kDenseThreads * kDenseStride];
+  __shared__ unsigned s_cnt[kSortBins];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t first = int64_t(blockIdx.x) * kDenseThreads + warp * 32;  // the warp's first matrix
+  float* sw = s_m + warp * 32 * kDenseStride;
+  float4 v[16];
 #pragma unroll
-    for (int t = 0; t < P; ++t) {
-      nrow = fmax(nrow, row[t]);
-      ncol = fmax(ncol, col[t]);
-    }
-    unsigned short key = kKeyBad;
-    if (!bad) {
-      int m, s;
-      choose_degree(fmin(nrow, ncol), &m, &s);
-      key = make_key(m, s);
-    }
+  for (int k = 0; k < 16; ++k) {
+    const int g = k * 32 + lane;  // chunk g of the warp's 512: matrix g / 16, chunk g % 16
+    v[k] = first + (g >> 4) < batch ? ld_f32x4(a + (first + (g >> 4)) * 64 + 4 * (g & 15))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int g = k * 32 + lane;
+    *reinterpret_cast<float4*>(sw + (g >> 4) * kDenseStride + 4 * (g & 15)) = v[k];
+  }
+  __syncwarp();
+  const int64_t b = first + lane;
+  int bin = -1;
+  if (b < batch) {
+    float4 x[8][2];
+#pragma unroll
+    for (int o = 0; o < 8; ++o)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) x[o][q] = *reinterpret_cast<const float4*>(sw + lane * kDenseStride + 8 * o + 4 * q);
+    const unsigned short key = key_of_matrix<8>(x, (flags & kClsRows) != 0);
     ws.keys[b] = key;
     bin = key_bin(key);
   }

@@ -194,7 +194,17 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
     flags |= kClsVec;
   const int64_t blocks = (batch + kSortThreads - 1) / kSortThreads;
   if (blocks > 0x7fffffffLL) return FHX_ERR_SIZE;
-  classify_kernel<P><<<unsigned(blocks), kSortThreads, 0, stream>>>(a, batch, n, dtype, flags, w);
+  // dense float32 8 x 8 batch (rows or columns contiguous): the coalesced classification
+  const bool dense8 = P == 8 && n == 8 && dtype == kF32 && a.s0 == 64 &&
+                      ((a.s1 == 8 && a.s2 == 1) || (a.s1 == 1 && a.s2 == 8)) && aligned(a.data, 16);
+  if (dense8) {
+    const int64_t dblocks = (batch + kDenseThreads - 1) / kDenseThreads;
+    if (dblocks > 0x7fffffffLL) return FHX_ERR_SIZE;
+    classify_dense8_kernel<<<unsigned(dblocks), kDenseThreads, 0, stream>>>(static_cast<const float*>(a.data), batch,
+                                                                             flags, w);
+  } else {
+    classify_kernel<P><<<unsigned(blocks), kSortThreads, 0, stream>>>(a, batch, n, dtype, flags, w);
+  }
   scatter_kernel<<<unsigned(blocks), kSortThreads, 0, stream>>>(batch, w);
   note_launches(2);
   st = cuda_status(cudaGetLastError());
