@@ -85,24 +85,37 @@ __device__ __forceinline__ RMat<N, Pair> rident(float c0) {
   return r;
 }
 
-// r += c * x
+// r += c * x, element pairs with one paired FMA (FFMA2: two independent round-to-nearest FMAs,
+// the same bits as fmaf on each element).
+__device__ __forceinline__ void axpy_plane(float* r, float c, const float* x, int count) {
+#pragma unroll
+  for (int e = 0; e + 1 < count; e += 2) {
+    const float2 v = __ffma2_rn(make_float2(c, c), make_float2(x[e], x[e + 1]), make_float2(r[e], r[e + 1]));
+    r[e] = v.x;
+    r[e + 1] = v.y;
+  }
+  if (count & 1) r[count - 1] = fmaf(c, x[count - 1], r[count - 1]);
+}
 template <int N, bool Pair>
 __device__ __forceinline__ void raxpy(RMat<N, Pair>& r, float c, const RMat<N, Pair>& x) {
-#pragma unroll
-  for (int e = 0; e < N * N; ++e) {
-    r.d[e] = fmaf(c, x.d[e], r.d[e]);
-    if constexpr (Pair) r.u[e] = fmaf(c, x.u[e], r.u[e]);
-  }
+  axpy_plane(r.d, c, x.d, N * N);
+  if constexpr (Pair) axpy_plane(r.u, c, x.u, N * N);
 }
 
-// r += x
+// r += x (paired adds, as above)
+__device__ __forceinline__ void add_plane(float* r, const float* x, int count) {
+#pragma unroll
+  for (int e = 0; e + 1 < count; e += 2) {
+    const float2 v = __fadd2_rn(make_float2(r[e], r[e + 1]), make_float2(x[e], x[e + 1]));
+    r[e] = v.x;
+    r[e + 1] = v.y;
+  }
+  if (count & 1) r[count - 1] += x[count - 1];
+}
 template <int N, bool Pair>
 __device__ __forceinline__ void radd(RMat<N, Pair>& r, const RMat<N, Pair>& x) {
-#pragma unroll
-  for (int e = 0; e < N * N; ++e) {
-    r.d[e] += x.d[e];
-    if constexpr (Pair) r.u[e] += x.u[e];
-  }
+  add_plane(r.d, x.d, N * N);
+  if constexpr (Pair) add_plane(r.u, x.u, N * N);
 }
 
 // Linear combination c[0] I + c[1] b1 + c[2] b2 + ... over up to four matrices.
