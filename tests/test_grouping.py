@@ -157,3 +157,33 @@ def test_cabi_frechet_grouped(n):
     torch.cuda.synchronize()
     assert torch.equal(l_reuse, l_fresh)
     assert O.per_matrix_error(l_reuse, O.frechet_fp64(at, e)).max() <= O.tolerance("float32", True)
+
+
+def test_grouping_handoff_only_inside_autograd():
+    """Direct operator calls never take a grouping left elsewhere: each _frechet call groups
+    afresh (two grouping passes and the main kernel), also right after a _matrix_exp call on the
+    same tensor, and an autograd forward whose backward never runs leaves nothing behind."""
+    from .conftest import count_fhx_launches, grouping_passes
+
+    n = 8
+    a = _mixed(512, n, torch.float32, 31)
+    g = torch.randn(512, n, n).cuda()
+    ops = torch.ops.flash_hypercons
+    assert count_fhx_launches(lambda: ops._matrix_exp(a)) == 1 + grouping_passes(n)
+    assert count_fhx_launches(lambda: ops._frechet(a.mT, g)) == 1 + grouping_passes(n)
+    x = a.detach().requires_grad_()
+    fh.matrix_exp(x)  # graph dropped without a backward
+    assert count_fhx_launches(lambda: ops._frechet(a.mT, g)) == 1 + grouping_passes(n)
+
+
+def test_input_changed_before_backward_raises():
+    """The reused grouping belongs to the saved input; autograd refuses a backward after the
+    input changed in place, so stale keys are never used."""
+    a = _mixed(256, 8, torch.float32, 33)
+    g = torch.randn(256, 8, 8).cuda()
+    x = a.clone().requires_grad_()
+    y = fh.matrix_exp(x)
+    with torch.no_grad():
+        x.mul_(3.0)
+    with pytest.raises(RuntimeError, match="modified by an inplace operation"):
+        torch.autograd.grad(y, x, g)
