@@ -231,6 +231,17 @@ __device__ __forceinline__ int pidx(int i, int j) {
   return prow<P, TM>(i) * P + ((((j >> 2) ^ (i >> 2)) & (P / 4 - 1)) << 2) + (j & 3);
 }
 
+// The row whose |a| sum thread l of the norm phase takes.  At P = 32 rows 4 (l % 8) + l / 8, so
+// that the eight threads of a quarter-warp read rows of different chunk rotations (consecutive
+// rows share one, and their 128-bit reads collided 4-way): 32 x 32 forward 2.8 % and Frechet
+// 0.4 % faster on B200.  A permutation of the rows; only the maximum of the row sums is used.
+// (At P = 16 the same idea, rows 4 (l % 4) + l / 4, measured 1.2 % slower on the forward.)
+template <int P>
+__device__ __forceinline__ int norm_row(int l) {
+  if constexpr (P == 32) return 4 * (l & 7) + (l >> 3);
+  return l;
+}
+
 template <int T>
 __device__ __forceinline__ void team_sync(int team_in_cta) {
   if constexpr (T <= 32) {
@@ -820,13 +831,13 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
       };
       if constexpr (T > 32) {
         if (t < P) {
-          nrow = row_sum(t);
+          nrow = row_sum(norm_row<P>(t));
         } else if (t < 2 * P) {
           ncol = line_sum(t - P, true);
         }
       } else {
         for (int l = t; l < P; l += T) {
-          nrow = fmax(nrow, row_sum(l));
+          nrow = fmax(nrow, row_sum(norm_row<P>(l)));
           ncol = fmax(ncol, line_sum(l, true));
         }
       }
