@@ -687,13 +687,19 @@ __device__ __forceinline__ int ld_s32(const int* p) {
 // out: the result (exp(A), or L(A, E) for Frechet launches); out2 (Frechet launches only,
 // may be null): exp(A) of the same launch -- the value part of the pair -- transposed when
 // flags has kOut2T.
-// Grouped (perm, keys set; expm_sort.cuh): the team's k-th matrix is perm[k] instead of k, and
-// its (m, s) comes from keys[perm[k]] instead of the in-kernel norms; no degree is shared between
-// teams.  A template parameter, so that the ungrouped kernel carries none of it in registers.
-template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped>
+// Grouped (keys set; expm_sort.cuh): each matrix's (m, s) comes from its key instead of the
+// in-kernel norms, and no degree is shared between teams.  With perm (the 5 <= n <= 8 grouping)
+// the team's k-th matrix is perm[k] instead of k and its key keys[perm[k]]; without (keyed mode,
+// the keys a forward launch stored) it is matrix k with key keys[k].  A template parameter, so
+// that the ungrouped kernel carries none of it in registers.
+// KeysOut (ungrouped launches): every matrix's key, make_key(m, s) or kKeyBad, is stored in
+// keys_out for a later keyed launch on the same matrices or their transposes.  A separate
+// instantiation, so that the other launches compile as without it.
+template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped, bool KeysOut = false>
 __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, WARPS>())) expm_team_kernel(View a, View e, void* __restrict__ out,
                                                                   void* __restrict__ out2, const int* __restrict__ perm,
                                                                   const unsigned short* __restrict__ keys,
+                                                                  unsigned short* __restrict__ keys_out,
                                                                   int64_t batch, int n, int dtype, unsigned flags) {
   const bool a_rows = flags & kARows, a_vec = flags & kAVec;
   const bool e_rows = flags & kERows, e_vec = flags & kEVec;
@@ -734,8 +740,10 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     bool ok = nb < batch;
     if constexpr (grouped) {
       if (ok) {
-        nb = ld_s32(perm + nb);
-        ok = nb >= 0 && nb < batch;  // an entry outside the batch (a foreign workspace) is skipped
+        if (perm != nullptr) {
+          nb = ld_s32(perm + nb);
+          ok = nb >= 0 && nb < batch;  // an entry outside the batch (a foreign workspace) is skipped
+        }
         pf_key = ok ? ld_u16(keys + nb) : 0u;
       }
       pf_b = ok ? nb : -1;
@@ -881,6 +889,10 @@ __global__ void __launch_bounds__(WARPS * 32, (team_min_blocks<P, TM, TN, Pair, 
     }
     const bool team_bad = nsteps < 0;
     if (team_bad) nsteps = 0;
+    if constexpr (KeysOut && !grouped) {
+      // every lane of the team stores the same key (one transaction, no divergent branch)
+      if (valid) keys_out[b] = team_bad ? kKeyBad : make_key(m, s);
+    }
     const int poly = scheme_products(m);
     const int prog = program_offset(m);
     if constexpr (T <= 32) team_sync<T>(tic);  // every column read is done before tiles are rescaled

@@ -138,15 +138,16 @@ unsigned layout_flags(const View& a, const View& e, const void* out, const void*
 
 // TM x TN: a thread's register tile; WARPS: warps per CTA.  A team is (P/TM) * (P/TN)
 // threads; one CTA holds WARPS * 32 / team-size teams.
-template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped>
+template <int P, int TM, int TN, bool Pair, int WARPS, bool Grouped, bool KeysOut = false>
 int launch_team_kernel(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n,
-                       int dtype, cudaStream_t stream, const int* perm, const unsigned short* keys) {
+                       int dtype, cudaStream_t stream, const int* perm, const unsigned short* keys,
+                       unsigned short* keys_out) {
   using C = TeamCfg<P, TM, TN, Pair>;
   constexpr int threads = WARPS * 32;
   constexpr int teams = threads / C::T;
   constexpr size_t smem = size_t(teams) * C::TEAM_FLOATS * sizeof(float);
   static LaunchShape shape;
-  auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS, Grouped>;
+  auto kernel = expm_team_kernel<P, TM, TN, Pair, WARPS, Grouped, KeysOut>;
   int dev = 0;
   const int st = cuda_status(cudaGetDevice(&dev));
   if (st != FHX_OK) return st;
@@ -157,23 +158,30 @@ int launch_team_kernel(const View& a, const View& e, void* out, void* out2, bool
   const int64_t items = (batch + teams - 1) / teams;
   const int64_t resident = int64_t(sms) * per_sm;
   const int blocks = int(items < resident ? items : resident);
-  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, perm, keys, batch, n, dtype,
+  kernel<<<blocks, threads, smem, stream>>>(a, e, out, out2, perm, keys, keys_out, batch, n, dtype,
                                             layout_flags<P>(a, e, out, out2, out2_t, n, dtype, Pair));
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
-// grouped (may be null): the permutation and keys of group_by_degree (P <= 16 only).
+// grouped (may be null): the keys of every matrix, with the permutation of group_by_degree
+// (P = 8) or without one (the 16 x 16 Frechet kernel: keyed mode, the keys a forward launch
+// stored); keys_out (may be null; the 16 x 16 forward only): store every matrix's key there.
 template <int P, int TM, int TN, bool Pair, int WARPS>
 int launch_team(const View& a, const View& e, void* out, void* out2, bool out2_t, int64_t batch, int n, int dtype,
-                cudaStream_t stream, const SortWorkspace* grouped = nullptr) {
-  if constexpr (P == 8) {
+                cudaStream_t stream, const SortWorkspace* grouped = nullptr, unsigned short* keys_out = nullptr) {
+  if constexpr (P == 8 || (P == 16 && Pair)) {
     if (grouped != nullptr)
       return launch_team_kernel<P, TM, TN, Pair, WARPS, true>(a, e, out, out2, out2_t, batch, n, dtype, stream,
-                                                              grouped->perm, grouped->keys);
+                                                              grouped->perm, grouped->keys, nullptr);
+  }
+  if constexpr (P == 16 && !Pair) {
+    if (keys_out != nullptr)
+      return launch_team_kernel<P, TM, TN, Pair, WARPS, false, true>(a, e, out, out2, out2_t, batch, n, dtype, stream,
+                                                                     nullptr, nullptr, keys_out);
   }
   return launch_team_kernel<P, TM, TN, Pair, WARPS, false>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr,
-                                                           nullptr);
+                                                           nullptr, nullptr);
 }
 
 // Grouping passes of expm_sort.cuh on the view `a` (5 <= n <= 8): keys, histogram and permutation in
@@ -241,6 +249,7 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
   // whose 254 registers left 8 warps per SM).
   SortWorkspace ws{};
   const SortWorkspace* grouped = nullptr;
+  unsigned short* keys_out = nullptr;
   if (workspace != nullptr && grouped_size(n)) {
     if (reuse_grouping) {
       ws = sort_workspace(workspace, batch);
@@ -249,6 +258,18 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
       if (st != FHX_OK) return st;
     }
     grouped = &ws;
+  } else if (workspace != nullptr && n > 8 && n <= 16) {
+    // 9 <= n <= 16: the workspace holds one key per matrix; the forward stores them and the
+    // Frechet launch of fhx_frechet_grouped reads them (keyed mode, no norm phase: measured
+    // 5.6 % off the 16 x 16 Frechet kernel, against 3.7 % more for the forward that stores them;
+    // at 32 x 32 the keyed kernel measured no faster, so 17 <= n <= 32 keeps its norm phase)
+    if (Pair && reuse_grouping) {
+      ws.keys = static_cast<unsigned short*>(workspace);
+      ws.perm = nullptr;
+      grouped = &ws;
+    } else if (!Pair) {
+      keys_out = static_cast<unsigned short*>(workspace);
+    }
   }
 #if FHX_FRECHET8_TILE == 24
   if constexpr (Pair) {
@@ -261,24 +282,24 @@ int dispatch(const View& a, const View& e, void* out, int64_t batch, int n, int 
     if constexpr (Pair) {
       return launch_team<16, 2, 4, true, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
     } else {
-      return launch_team<16, 4, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
+      return launch_team<16, 4, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr, keys_out);
     }
   }
   if constexpr (Pair) {
 #if FHX_FRECHET32_TILE == 4
-    return launch_team<32, 4, 4, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 4, 4, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
 #elif FHX_FRECHET32_TILE == 28
-    return launch_team<32, 2, 8, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 2, 8, true, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
 #else
-    return launch_team<32, 2, 4, true, 4>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 2, 4, true, 4>(a, e, out, out2, out2_t, batch, n, dtype, stream, grouped);
 #endif
   } else {
 #if FHX_FORWARD32_TILE == 48
-    return launch_team<32, 4, 8, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 4, 8, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr, keys_out);
 #elif FHX_FORWARD32_TILE == 84
-    return launch_team<32, 8, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 8, 4, false, 1>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr, keys_out);
 #else
-    return launch_team<32, 4, 4, false, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream);
+    return launch_team<32, 4, 4, false, 2>(a, e, out, out2, out2_t, batch, n, dtype, stream, nullptr, keys_out);
 #endif
   }
 }
@@ -371,8 +392,9 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
 }
 
 size_t fhx_workspace_bytes(int64_t batch, int32_t n) {
-  if (batch <= 0 || !fhx::grouped_size(n)) return 0;
-  return fhx::sort_workspace_bytes(batch);
+  if (batch <= 0 || n < 5 || n > 16) return 0;
+  if (fhx::grouped_size(n)) return fhx::sort_workspace_bytes(batch);
+  return fhx::align256(size_t(batch) * sizeof(unsigned short));  // one key per matrix
 }
 
 int32_t fhx_matrix_exp_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
@@ -492,7 +514,7 @@ int32_t fhx_last_cuda_error(void) { return static_cast<int32_t>(fhx::g_last_cuda
 
 const char* fhx_last_cuda_error_string(void) { return cudaGetErrorString(fhx::g_last_cuda_error); }
 
-int32_t fhx_abi_version(void) { return 105; }
+int32_t fhx_abi_version(void) { return 106; }
 
 uint64_t fhx_launch_count(void) { return fhx::g_launches.load(std::memory_order_relaxed); }
 

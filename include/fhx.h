@@ -76,8 +76,10 @@ int32_t fhx_frechet(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_
                     void* output, int64_t batch, int32_t n, int32_t dtype, void* stream);
 
 /*
- * Device workspace (bytes) that fhx_matrix_exp_ws / fhx_frechet_ws / fhx_matrix_exp_frechet need
- * for a batch of n x n matrices: 6 bytes per matrix plus 2 KB for 5 <= n <= 8, 0 otherwise.
+ * Device workspace (bytes) that fhx_matrix_exp_ws / fhx_frechet_ws / fhx_frechet_grouped /
+ * fhx_matrix_exp_frechet need for a batch of n x n matrices: 6 bytes per matrix plus 2 KB for
+ * 5 <= n <= 8 (the degree grouping), 2 bytes per matrix rounded up to 256 for 9 <= n <= 16 (one
+ * key per matrix), 0 otherwise.
  */
 size_t fhx_workspace_bytes(int64_t batch, int32_t n);
 
@@ -89,8 +91,10 @@ size_t fhx_workspace_bytes(int64_t batch, int32_t n);
  * squarings) -- two small passes that classify every matrix in float64 and build a
  * permutation -- so that the matrices of a warp run the same program, and every matrix runs its
  * own degree: its result depends on that matrix alone (bit-stable under any batching), and
- * fhx_frechet_ws on A^T repeats the (m, s) of fhx_matrix_exp_ws on A exactly.  Other n ignore
- * the workspace (workspace_bytes may be 0); they are per-matrix already.
+ * fhx_frechet_ws on A^T repeats the (m, s) of fhx_matrix_exp_ws on A exactly.  Other n are
+ * per-matrix already; for 9 <= n <= 16 fhx_matrix_exp_ws stores each matrix's key -- its
+ * (m, s) -- in the workspace for a later fhx_frechet_grouped, and fhx_frechet_ws does not use it.
+ * n <= 4 and n >= 17 need no workspace (workspace_bytes may be 0).
  * Reference interfaces: as fhx_matrix_exp / fhx_frechet (the workspace replaces the
  * reference's per-call pre-copies, csrc/matrix_exp.cu:35-44, which the caching allocator
  * provides there).
@@ -108,12 +112,13 @@ int32_t fhx_frechet_ws(const void* input, int64_t in_s0, int64_t in_s1, int64_t 
  * (or their transposes: the classification of A and A^T is identical), same batch and n.  An
  * extension without reference counterpart, for the autograd backward: exp(X) on X, then
  * L(X^T, dY) on X^T, with the forward's workspace kept until the backward.  For 5 <= n <= 8 the
- * grouping passes are skipped and every matrix runs the forward's (m, s) from the stored
- * keys; the kernels only read the workspace.  Results equal fhx_frechet_ws's bit for bit.  The
- * caller guarantees that the workspace holds that grouping and that the matrices were not
- * changed in between: a workspace of other matrices gives wrong results (permutation entries
- * outside [0, batch) are skipped, so nothing is read or written out of bounds).  Other n ignore
- * the workspace.
+ * grouping passes are skipped, and for 9 <= n <= 16 the kernel's norm phase: every matrix runs
+ * the forward's (m, s) from the stored keys; the kernels only read the workspace.  Results
+ * equal fhx_frechet_ws's bit for bit.  The caller guarantees that the workspace holds those
+ * keys and that the matrices were not changed in between: a workspace of other matrices gives
+ * wrong results (permutation entries outside [0, batch) are skipped, so nothing is read or
+ * written out of bounds).  n <= 4 and n >= 17 ignore the workspace (their backward recomputes
+ * the same (m, s) from A^T).
  */
 int32_t fhx_frechet_grouped(const void* input, int64_t in_s0, int64_t in_s1, int64_t in_s2, int32_t in_negate,
                             const void* direction, int64_t dir_s0, int64_t dir_s1, int64_t dir_s2,

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_cabi()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.fhx_abi_version() == 105
+    assert lib.fhx_abi_version() == 106
 
 
 def test_status_strings():
@@ -73,8 +73,10 @@ def test_workspace_sizes_and_errors_without_gpu():
     # 6 bytes per matrix (key + permutation entry) plus the bin tables, for 5 <= n <= 8 only
     assert lib.fhx_workspace_bytes(1000, 8) >= 6000
     assert lib.fhx_workspace_bytes(1000, 8) == lib.fhx_workspace_bytes(1000, 5)
-    assert lib.fhx_workspace_bytes(1000, 4) == 0 and lib.fhx_workspace_bytes(1000, 9) == 0
-    assert lib.fhx_workspace_bytes(1000, 16) == 0 and lib.fhx_workspace_bytes(1000, 17) == 0
+    assert lib.fhx_workspace_bytes(1000, 4) == 0 and lib.fhx_workspace_bytes(1000, 2) == 0
+    # one 2-byte key per matrix for 9 <= n <= 16, rounded up to 256 bytes
+    assert lib.fhx_workspace_bytes(1000, 9) == 2048 and lib.fhx_workspace_bytes(1000, 16) == 2048
+    assert lib.fhx_workspace_bytes(1000, 17) == 0 and lib.fhx_workspace_bytes(1000, 32) == 0
     assert lib.fhx_workspace_bytes(0, 8) == 0
     buf = ctypes.c_void_p(256)
     need = lib.fhx_workspace_bytes(64, 8)
