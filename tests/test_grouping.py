@@ -188,3 +188,42 @@ def test_input_changed_before_backward_raises():
         x.mul_(3.0)
     with pytest.raises(RuntimeError, match="modified by an inplace operation"):
         torch.autograd.grad(y, x, g)
+
+
+def test_handoff_with_concurrent_threads():
+    """Forward + backward from several Python threads at once (each on its own stream; the
+    autograd engine runs all of their backward calls on one worker thread per device): every
+    thread's gradient equals the one computed alone, so no grouping or key crosses over."""
+    import threading
+
+    cases = []
+    for i, n in enumerate((6, 8, 12, 16)):
+        a = _mixed(3000, n, torch.float32, 40 + i)
+        g = torch.randn(3000, n, n, generator=torch.Generator().manual_seed(50 + i)).cuda()
+        cases.append((a, g, _fwd_bwd(a, g)))
+    torch.cuda.synchronize()
+    results = [None] * len(cases)
+    errors = []
+
+    def work(k):
+        try:
+            a, g, _ = cases[k]
+            stream = torch.cuda.Stream()
+            outs = []
+            with torch.cuda.stream(stream):
+                for _ in range(20):
+                    outs.append(_fwd_bwd(a, g))
+            stream.synchronize()
+            results[k] = outs
+        except Exception as exc:  # surfaced below
+            errors.append(exc)
+
+    threads = [threading.Thread(target=work, args=(k,)) for k in range(len(cases))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    for (a, g, (y0, g0)), outs in zip(cases, results):
+        for y, grad in outs:
+            assert torch.equal(y, y0) and torch.equal(grad, g0)
