@@ -215,39 +215,47 @@ __global__ void __launch_bounds__(kSortThreads) classify_kernel(View a, int64_t 
 constexpr int kDenseThreads = 128;
 constexpr int kDenseStride = 68;  // floats per matrix in shared memory (64 + 4 of padding)
 
-__global__ void __launch_bounds__(kDenseThreads) classify_dense8_kernel(const float* __restrict__ a, int64_t batch,
+__global__ void __launch_bounds__(kDenseThreads, 5) classify_dense8_kernel(const float* __restrict__ a, int64_t batch,
                                                                         unsigned flags, SortWorkspace ws) {
   __shared__ __align__(16) float s_m[kDenseThreads * kDenseStride];
   __shared__ unsigned s_cnt[kSortBins];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t first = int64_t(blockIdx.x) * kDenseThreads + warp * 32;  // the warp's first matrix
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
   float* sw = s_m + warp * 32 * kDenseStride;
-  float4 v[16];
+  // Tiles of kDenseThreads matrices, grid-strided: one histogram flush per CTA, not per tile.
+  for (int64_t tile = blockIdx.x; tile * kDenseThreads < batch; tile += gridDim.x) {
+    const int64_t first = tile * kDenseThreads + warp * 32;  // the warp's first matrix
+    float4 v[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int g = k * 32 + lane;  // chunk g of the warp's 512: matrix g / 16, chunk g % 16
-    v[k] = first + (g >> 4) < batch ? ld_f32x4(a + (first + (g >> 4)) * 64 + 4 * (g & 15))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < 16; ++k) {
+      const int g = k * 32 + lane;  // chunk g of the warp's 512: matrix g / 16, chunk g % 16
+      v[k] = first + (g >> 4) < batch ? ld_f32x4(a + (first + (g >> 4)) * 64 + 4 * (g & 15))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncwarp();  // the previous tile's reads of this warp's region are done
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int g = k * 32 + lane;
+      *reinterpret_cast<float4*>(sw + (g >> 4) * kDenseStride + 4 * (g & 15)) = v[k];
+    }
+    __syncwarp();
+    const int64_t b = first + lane;
+    if (b < batch) {
+      float4 x[8][2];
+#pragma unroll
+      for (int o = 0; o < 8; ++o)
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          x[o][q] = *reinterpret_cast<const float4*>(sw + lane * kDenseStride + 8 * o + 4 * q);
+      const unsigned short key = key_of_matrix<8>(x, (flags & kClsRows) != 0);
+      ws.keys[b] = key;
+      atomicAdd(&s_cnt[key_bin(key)], 1u);
+    }
   }
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int g = k * 32 + lane;
-    *reinterpret_cast<float4*>(sw + (g >> 4) * kDenseStride + 4 * (g & 15)) = v[k];
-  }
-  __syncwarp();
-  const int64_t b = first + lane;
-  int bin = -1;
-  if (b < batch) {
-    float4 x[8][2];
-#pragma unroll
-    for (int o = 0; o < 8; ++o)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) x[o][q] = *reinterpret_cast<const float4*>(sw + lane * kDenseStride + 8 * o + 4 * q);
-    const unsigned short key = key_of_matrix<8>(x, (flags & kClsRows) != 0);
-    ws.keys[b] = key;
-    bin = key_bin(key);
-  }
-  add_block_histogram(bin, ws.hist, s_cnt);
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSortBins; i += blockDim.x)
+    if (s_cnt[i]) atomicAdd(&ws.hist[i], s_cnt[i]);
 }
 
 // Exclusive prefix sum of the kSortBins histogram counts into s_start, by every CTA of the scatter

@@ -21,6 +21,9 @@
 #ifndef FHX_FORWARD32_TILE
 #define FHX_FORWARD32_TILE 44
 #endif
+#ifndef FHX_DENSE_CTAS_PER_SM
+#define FHX_DENSE_CTAS_PER_SM 5
+#endif
 #ifndef FHX_FRECHET8_TILE
 #define FHX_FRECHET8_TILE 24
 #endif
@@ -206,8 +209,14 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
   const bool dense8 = P == 8 && n == 8 && dtype == kF32 && a.s0 == 64 &&
                       ((a.s1 == 8 && a.s2 == 1) || (a.s1 == 1 && a.s2 == 8)) && aligned(a.data, 16);
   if (dense8) {
-    const int64_t dblocks = (batch + kDenseThreads - 1) / kDenseThreads;
-    if (dblocks > 0x7fffffffLL) return FHX_ERR_SIZE;
+    // at most FHX_DENSE_CTAS_PER_SM resident CTAs per SM, each looping over tiles
+    int dev = 0;
+    st = cuda_status(cudaGetDevice(&dev));
+    if (st != FHX_OK) return st;
+    if (dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
+    const int64_t tiles = (batch + kDenseThreads - 1) / kDenseThreads;
+    const int64_t cap = int64_t(device_sms(dev)) * FHX_DENSE_CTAS_PER_SM;
+    const int64_t dblocks = tiles < cap ? tiles : cap;
     classify_dense8_kernel<<<unsigned(dblocks), kDenseThreads, 0, stream>>>(static_cast<const float*>(a.data), batch,
                                                                              flags, w);
   } else {
