@@ -216,6 +216,7 @@ int group_by_degree(const View& a, int64_t batch, int n, int dtype, void* worksp
     if (dev < 0 || dev >= kMaxDevices) return FHX_ERR_CUDA;
     const int64_t tiles = (batch + kDenseThreads - 1) / kDenseThreads;
     const int64_t cap = int64_t(device_sms(dev)) * FHX_DENSE_CTAS_PER_SM;
+    if (cap <= 0) return FHX_ERR_CUDA;
     const int64_t dblocks = tiles < cap ? tiles : cap;
     classify_dense8_kernel<<<unsigned(dblocks), kDenseThreads, 0, stream>>>(static_cast<const float*>(a.data), batch,
                                                                              flags, w);
