@@ -182,15 +182,18 @@ struct TeamCfg {
   static constexpr int PLANE = P * P;
   static constexpr int NPART = Pair ? 2 : 1;
   static constexpr int SLOT = NPART * PLANE;
-  // Teams that share a warp start in different banks; 4 floats of per-team scratch.
-  // Teams that share a warp start 16 banks apart (P = 8 and 16 alike).
-  static constexpr int SKEW = T >= 32 ? 0 : 16;
+  // Teams that share a warp start in different banks (4 floats of per-team scratch included):
+  // 16 banks apart, except the four 8-thread teams of the 8 x 8 Frechet kernel, which start 8
+  // apart and so cover all four offsets (measured 1.2-1.5 % faster on config 3; the eight 4 x 4
+  // forward teams ran 5 % slower at 8 apart).
+  static constexpr int SKEW = T >= 32 ? 0 : (P == 8 && T == 8 ? 8 : 16);
   static constexpr int TEAM_FLOATS = kSlots * SLOT + 4 + (SKEW ? SKEW - 4 : 12);
   static_assert(32 % T == 0 || (T % 32 == 0 && T <= 256), "team must divide a warp or be whole warps");
   // Thread -> tile map: each quarter-warp (8 threads) covers QR row blocks x QC column
-  // blocks.  A 128-bit shared load costs 2 wavefronts when every quarter-warp touches at
-  // most two distinct 16-byte chunks and 4 otherwise (measured), so the more frequent load
-  // (X blocks: TM per k-group, Y rows: TN per k-group) gets the quarter with <= 2 chunks.
+  // blocks, and the chunks it reads together fall in distinct bank groups.  Measured on B200
+  // (ncu shared-load wavefronts): a 128-bit load costs 2 wavefronts per warp both when every
+  // quarter-warp reads the same four chunks (the X blocks of the 32 x 32 kernels) and when each
+  // reads two and the warp eight (their Y rows); different chunks in one bank group cost more.
   static constexpr int QR = (T < 8) ? 1 : (TN >= TM ? (RB >= 4 ? 4 : RB) : 2);
   static constexpr int QC = (T < 8) ? 1 : 8 / QR;
   static_assert(T < 8 || (RB % QR == 0 && CB % QC == 0 && QR * QC == 8), "quarter-warp tiling");
