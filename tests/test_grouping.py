@@ -105,7 +105,7 @@ def test_grouped_nonfinite_and_degree_one():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("n", [5, 8, 12, 16, 24, 32])
+@pytest.mark.parametrize("n", [5, 7, 8, 9, 12, 13, 16, 24, 32])
 @pytest.mark.parametrize("layout", ["contiguous", "transposed"])
 def test_backward_reuses_forward_grouping(n, dtype, layout):
     """The autograd backward takes the forward's grouping (5 <= n <= 8) or keys (9 <= n <= 16;
@@ -133,7 +133,7 @@ def test_backward_reuses_forward_grouping(n, dtype, layout):
     assert torch.equal(g1, fresh) and torch.equal(g2, fresh)
 
 
-@pytest.mark.parametrize("n", [5, 8, 12, 16, 24, 32])
+@pytest.mark.parametrize("n", [5, 7, 8, 9, 12, 13, 16, 24, 32])
 def test_cabi_frechet_grouped(n):
     """fhx_frechet_grouped on A^T with the workspace of fhx_matrix_exp_ws on A equals
     fhx_frechet_ws (which groups afresh) bit for bit."""
