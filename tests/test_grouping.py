@@ -227,3 +227,16 @@ def test_handoff_with_concurrent_threads():
     for (a, g, (y0, g0)), outs in zip(cases, results):
         for y, grad in outs:
             assert torch.equal(y, y0) and torch.equal(grad, g0)
+
+
+@pytest.mark.parametrize("n", [6, 12])
+@pytest.mark.parametrize("batch", [1, 3, 33])
+def test_reuse_tiny_batches(n, batch):
+    """Grouping / key reuse on batches smaller than a CTA's teams: the autograd gradient equals a
+    fresh _frechet call bit for bit and passes the float64 oracle."""
+    a = _mixed(batch, n, torch.float32, 60 + batch)
+    g = torch.randn(batch, n, n, generator=torch.Generator().manual_seed(70 + batch)).cuda()
+    y, grad = _fwd_bwd(a, g)
+    assert torch.equal(grad, torch.ops.flash_hypercons._frechet(a.mT, g))
+    assert O.per_matrix_error(y, O.exp_fp64(a)).max() <= O.tolerance("float32", False)
+    assert O.per_matrix_error(grad, O.frechet_fp64(a.mT, g)).max() <= O.tolerance("float32", True)
